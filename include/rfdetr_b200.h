@@ -1,0 +1,122 @@
+/* rfdetr_b200.h — additive entry points of the B200 engine.
+ *
+ * The reference API (rfdetr.h) is batch-1 and single-device: one image per
+ * rfdetr_detect call, with the model forward at src/rfdetr_model.cpp:77
+ * (rfdetr_model_forward: one preprocessed image -> ForwardOutput).  The
+ * functions below are the batched / device-placed replacements of that seam;
+ * they are additions, none of the reference symbols change.  Contexts created
+ * here are ordinary rfdetr_context objects (rfdetr_detect, rfdetr_free and the
+ * accessors all work on them).  A context owns one GPU and one CUDA stream and
+ * is not re-entrant: use one context per host thread.
+ */
+#ifndef RFDETR_B200_H
+#define RFDETR_B200_H
+
+#include "rfdetr.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    int device;     /* CUDA device ordinal (default 0) */
+    int max_batch;  /* images the activation arena is sized for at init (grows on demand) */
+} rfdetr_b200_params;
+
+/* Replaces rfdetr_init (src/rfdetr.cpp:37-107) with an explicit device and
+ * batch capacity.  `b200` may be NULL (device 0, batch 1). */
+rfdetr_context* rfdetr_b200_init(const rfdetr_params* params, const rfdetr_b200_params* b200,
+                                 rfdetr_status* out_status);
+
+/* Batched rfdetr_model_forward (src/rfdetr_model.hpp:52-60) from host uint8
+ * RGB images, `batch` images of width x height, HWC, contiguous.  Images are
+ * resized / normalized on the GPU exactly like rfdetr_preprocess
+ * (src/image_io.cpp:207-248).  Outputs (host, may be NULL):
+ *   out_logits [batch][num_queries][num_classes]  (class fastest)
+ *   out_boxes  [batch][num_queries][4]            normalized cx, cy, w, h
+ *   out_masks  [batch][num_queries][m][m]         seg models, m = mask side */
+rfdetr_status rfdetr_b200_forward_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width, int height,
+                                      float* out_logits, float* out_boxes, float* out_masks);
+
+/* Same, from already-preprocessed planar input [batch][3][S][S] (S = image
+ * size), i.e. exactly the `input` argument of rfdetr_model_forward. */
+rfdetr_status rfdetr_b200_forward_planar(rfdetr_context* ctx, const float* planar, int batch,
+                                         float* out_logits, float* out_boxes, float* out_masks);
+
+/* Device-resident path: `d_rgb` is a DEVICE pointer (on the context's GPU) to
+ * batch x height x width x 3 uint8.  Enqueues preprocess + forward on the
+ * context stream and returns without waiting; outputs stay on the device
+ * (rfdetr_b200_device_outputs).  rfdetr_b200_sync waits and reports device
+ * errors. */
+rfdetr_status rfdetr_b200_enqueue_device(rfdetr_context* ctx, const uint8_t* d_rgb, int batch, int width,
+                                         int height);
+rfdetr_status rfdetr_b200_sync(rfdetr_context* ctx);
+/* Device pointers of the last forward's outputs (layouts as above). */
+rfdetr_status rfdetr_b200_device_outputs(rfdetr_context* ctx, const float** d_logits, const float** d_boxes,
+                                         const float** d_masks);
+
+/* Batched rfdetr_detect: n images (any sizes) -> per-image detection arrays.
+ * out_dets[i] / out_counts[i] follow rfdetr_detect's ownership rules
+ * (free each with rfdetr_detections_free). */
+rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfdetr_image* const* imgs, size_t n,
+                                       const rfdetr_detect_params* params, rfdetr_detection** out_dets,
+                                       size_t* out_counts);
+
+int   rfdetr_b200_device(const rfdetr_context* ctx);
+int   rfdetr_b200_mask_side(const rfdetr_context* ctx);         /* 0 for detection models */
+int   rfdetr_b200_kernels_per_forward(const rfdetr_context* ctx);
+void* rfdetr_b200_stream(const rfdetr_context* ctx);              /* the context's cudaStream_t */
+
+/* Copy a named intermediate of the last forward to host as f32 (parity
+ * tests; names follow the reference's trace checkpoints, src/trace.cpp).
+ * Returns the element count, or -1 (unknown name / capacity too small). */
+long long rfdetr_b200_trace(rfdetr_context* ctx, const char* name, int batch, float* out, size_t cap);
+
+/* Host-only inspection of a GGUF file (no GPU needed), for loaders and tests:
+ * parses, validates the tensor inventory (src/model_loader.cpp:212-750) and
+ * checks that the engine implements the configuration. */
+typedef struct {
+    uint32_t image_size, patch_size, num_queries, num_classes;
+    uint32_t dim, depth, num_windows, dec_layers;
+    int      has_segmentation_head;
+    size_t   n_tensors;
+    char     variant[32];
+} rfdetr_b200_model_info;
+rfdetr_status rfdetr_b200_inspect(const char* model_path, rfdetr_b200_model_info* out);
+
+/* Host dequantizer of one GGUF tensor payload (ggml type id -> f32). Returns 0
+ * on success, -1 for an unsupported type. */
+int rfdetr_b200_dequantize(uint32_t ggml_type, const void* src, long long n, float* dst);
+
+/* ---- operator entry points (device pointers, asynchronous on `stream`) ----
+ * The engine's building blocks, exposed so callers can reuse them and so each
+ * kernel can be checked on its own.  `stream` is a cudaStream_t (NULL = the
+ * legacy default stream).  Return 0 on success, otherwise a cudaError_t code.
+ *
+ * GEMM: out = epilogue(A[M][K] . B[N][K]^T + bias) with f16 A / B (K
+ * contiguous, lda/ldb multiples of 8) and f32 accumulation on the tcgen05
+ * tensor cores.  epi: 0 f16 out, 1 f32 out, 2 f32 out += colscale * value,
+ * 4 full-row LayerNorm (N = 128 or 256) -> f32 and/or f16.  act: 0 none,
+ * 1 GELU (erf), 2 ReLU, 3 SiLU. */
+int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int epi, int act,
+                        const float* bias, const float* colscale, const float* ln_g, const float* ln_b,
+                        float ln_eps, const float* resid, int ldr, float* out32, int ld32, void* out16, int ld16,
+                        void* stream);
+
+/* Fused attention O = softmax(scale * Q K^T) V, f16 in / out, head_dim 32 or
+ * 64; rows of group g start at g * seq_len; head h uses columns
+ * [h*head_dim, (h+1)*head_dim) of each operand. */
+int rfdetr_b200_op_attention(const void* q, const void* k, const void* v, int ldq, int ldk, int ldv, void* o,
+                             int ldo, int seq_len, int groups, int heads, int head_dim, float scale, void* stream);
+
+/* Deformable sampling of one level (value f16 [B*G*G][Dm], so_aw f32
+ * [B*NQ][ld] = offsets (heads*points*2) then attention logits
+ * (heads*points), refpoints f32 [B*NQ][4]) -> out f16 [B*NQ][Dm]. */
+int rfdetr_b200_op_deform(const void* value, const float* so_aw, int ld_soaw, const float* refp, int batch, int nq,
+                          int grid, int heads, int points, int dm, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RFDETR_B200_H */

@@ -536,7 +536,7 @@ extern "C" void oracle_preprocess(const uint8_t* rgb, int w, int h, int tw, int 
 }
 
 extern "C" int oracle_forward(const OracleConfig* cfg, const OracleTensor* tensors, int n_tensors,
-                              const float* input, float* out_logits, float* out_boxes,
+                              const float* input, const int32_t* force_topk, float* out_logits, float* out_boxes,
                               int32_t* out_topk, float* out_masks,
                               oracle_publish_cb publish, void* user) {
 #ifdef _OPENMP
@@ -605,6 +605,11 @@ extern "C" int oracle_forward(const OracleConfig* cfg, const OracleTensor* tenso
         if (mx[a] != mx[b]) return mx[a] > mx[b];
         return a < b;
     });
+    if (force_topk)
+        for (int q = 0; q < NQ; ++q) {
+            if (force_topk[q] < 0 || force_topk[q] >= N) return -1;
+            idx[q] = force_topk[q];
+        }
     if (out_topk) for (int q = 0; q < NQ; ++q) out_topk[q] = idx[q];
 
     /* ---- decoder inputs (src/rfdetr_model.cpp:233-271) ---- */

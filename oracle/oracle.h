@@ -61,10 +61,13 @@ void oracle_preprocess(const uint8_t* rgb, int w, int h, int tw, int th,
 /* Full forward for one image.  input: planar [3][S][S].
  * out_logits [NQ][NC], out_boxes [NQ][4] (cx, cy, w, h), out_topk [NQ]
  * (selected token indices, may be NULL), out_masks [NQ][Hm][Wm] (seg only,
- * may be NULL).  Returns 0 on success, negative on a missing tensor or bad
+ * may be NULL).  force_topk (may be NULL) replaces the top-K selection with
+ * the given token indices, so the decoder can be compared on identical
+ * queries when near-tied scores order differently.  Returns 0 on success, negative on a missing tensor or bad
  * configuration. */
 int oracle_forward(const OracleConfig* cfg, const OracleTensor* tensors, int n_tensors,
-                   const float* input, float* out_logits, float* out_boxes,
+                   const float* input, const int32_t* force_topk,
+                   float* out_logits, float* out_boxes,
                    int32_t* out_topk, float* out_masks,
                    oracle_publish_cb publish, void* user);
 

@@ -52,7 +52,8 @@ def lib():
         L = C.CDLL(so)
         L.oracle_forward.restype = C.c_int
         L.oracle_forward.argtypes = [C.POINTER(OracleConfig), C.POINTER(OracleTensor), C.c_int,
-                                     C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_float),
+                                     C.POINTER(C.c_float), C.POINTER(C.c_int32),
+                                     C.POINTER(C.c_float), C.POINTER(C.c_float),
                                      C.POINTER(C.c_int32), C.POINTER(C.c_float), PUBLISH, C.c_void_p]
         L.oracle_preprocess.argtypes = [C.POINTER(C.c_uint8), C.c_int, C.c_int, C.c_int, C.c_int,
                                         C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_float)]
@@ -136,7 +137,8 @@ class Oracle:
                                 _fp(self.mean), _fp(self.std), _fp(out))
         return out
 
-    def forward(self, planar: np.ndarray, act_round: int = 0, trace: bool = False, n_threads: int = 0):
+    def forward(self, planar: np.ndarray, act_round: int = 0, trace: bool = False, n_threads: int = 0,
+                force_topk=None):
         cfg = config_from_meta(self.meta, act_round, n_threads)
         planar = np.ascontiguousarray(planar, dtype=np.float32)
         logits = np.zeros((self.nq, self.nc), np.float32)
@@ -149,7 +151,11 @@ class Oracle:
             store[name.decode()] = np.ctypeslib.as_array(data, shape=(n,)).copy()
 
         cb = PUBLISH(_pub) if trace else PUBLISH()
-        rc = lib().oracle_forward(C.byref(cfg), self._arr, len(self._names), _fp(planar),
+        ft = None
+        if force_topk is not None:
+            force_topk = np.ascontiguousarray(force_topk, np.int32)
+            ft = force_topk.ctypes.data_as(C.POINTER(C.c_int32))
+        rc = lib().oracle_forward(C.byref(cfg), self._arr, len(self._names), _fp(planar), ft,
                                   _fp(logits), _fp(boxes), topk.ctypes.data_as(C.POINTER(C.c_int32)),
                                   _fp(masks) if masks is not None else None, cb, None)
         if rc != 0:

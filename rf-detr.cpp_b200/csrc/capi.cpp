@@ -1,0 +1,503 @@
+// Public C ABI: rfdetr.h (context lifecycle, detect, accessors),
+// rfdetr_capi.h (flat handle API used by LocalAI) and rfdetr_b200.h (batched /
+// device entry points).  Semantics follow the reference's src/rfdetr.cpp and
+// src/rfdetr_capi.cpp: status codes, ownership, "clear the previous batch on
+// every detect call", two-call sizing.
+#include "rfdetr.h"
+#include "rfdetr_b200.h"
+#include "rfdetr_capi.h"
+
+#include "common.hpp"
+#include "engine.hpp"
+#include "image_io.hpp"
+#include "model.hpp"
+#include "postprocess.hpp"
+
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+struct rfdetr_context {
+    std::unique_ptr<rfb::Model> model;
+    std::unique_ptr<rfb::Engine> engine;
+    size_t n_tensors = 0;
+    int n_threads = 1;
+    // pinned host staging
+    uint8_t* h_in = nullptr;
+    size_t h_in_cap = 0;
+    float* h_out = nullptr;
+    size_t h_out_cap = 0;
+
+    ~rfdetr_context() {
+        if (h_in) cudaFreeHost(h_in);
+        if (h_out) cudaFreeHost(h_out);
+    }
+    bool stage_in(size_t bytes) {
+        if (bytes <= h_in_cap) return true;
+        if (h_in) cudaFreeHost(h_in);
+        h_in = nullptr;
+        h_in_cap = 0;
+        if (cudaMallocHost(&h_in, bytes) != cudaSuccess) return false;
+        h_in_cap = bytes;
+        return true;
+    }
+    bool stage_out(size_t floats) {
+        if (floats <= h_out_cap) return true;
+        if (h_out) cudaFreeHost(h_out);
+        h_out = nullptr;
+        h_out_cap = 0;
+        if (cudaMallocHost(&h_out, floats * 4) != cudaSuccess) return false;
+        h_out_cap = floats;
+        return true;
+    }
+};
+
+namespace {
+
+int resolve_threads(int n) {
+    if (n > 0) return n;
+    const unsigned hc = std::thread::hardware_concurrency();
+    return hc ? (int)hc : 1;
+}
+
+rfdetr_context* init_impl(const rfdetr_params* params, int device, int max_batch, rfdetr_status* out_status) {
+    auto set = [&](rfdetr_status s) { if (out_status) *out_status = s; };
+    if (!params || !params->model_path) { set(RFDETR_ERR_INVALID_ARG); return nullptr; }
+    if (params->log_cb) rfdetr_set_log_callback(params->log_cb, params->log_user_data);
+    rfdetr_status st;
+    std::unique_ptr<rfb::Model> m(rfb::model_load(params->model_path, &st));
+    if (!m) { set(st); return nullptr; }
+    st = rfb::model_validate(*m);
+    if (st != RFDETR_OK) { set(st); return nullptr; }
+    auto eng = rfb::Engine::create(*m, device, max_batch, &st);
+    if (!eng) { set(st); return nullptr; }
+    auto* ctx = new (std::nothrow) rfdetr_context();
+    if (!ctx) { set(RFDETR_ERR_OUT_OF_MEMORY); return nullptr; }
+    ctx->n_tensors = m->file.tensors.size();
+    m->file.data.clear();          // weights now live on the GPU
+    m->file.data.shrink_to_fit();
+    ctx->model = std::move(m);
+    ctx->engine = std::move(eng);
+    ctx->n_threads = resolve_threads(params->n_threads);
+    const rfb::Config& c = ctx->model->cfg;
+    rfdetr_logf(RFDETR_LOG_INFO, "rfdetr_init: loaded variant=%s, num_classes=%u, num_queries=%u, device=%d",
+                c.variant.c_str(), c.num_classes, c.num_queries, device);
+    set(RFDETR_OK);
+    return ctx;
+}
+
+// Copy the last forward's outputs for `batch` images to host buffers.
+rfdetr_status fetch_outputs(rfdetr_context* ctx, int batch, float* logits, float* boxes, float* masks) {
+    rfb::Engine& e = *ctx->engine;
+    const rfb::Config& c = e.cfg();
+    const size_t nq = c.num_queries, nc = c.num_classes;
+    cudaStream_t st = e.stream();
+    if (logits && RFB_CUDA_FAIL(cudaMemcpyAsync(logits, e.logits(), (size_t)batch * nq * nc * 4,
+                                                cudaMemcpyDeviceToHost, st)))
+        return RFDETR_ERR_INFERENCE;
+    if (boxes && RFB_CUDA_FAIL(cudaMemcpyAsync(boxes, e.boxes(), (size_t)batch * nq * 4 * 4, cudaMemcpyDeviceToHost, st)))
+        return RFDETR_ERR_INFERENCE;
+    if (masks && c.has_seg) {
+        const size_t hw = (size_t)e.mask_side() * e.mask_side();
+        if (RFB_CUDA_FAIL(cudaMemcpyAsync(masks, e.masks(), (size_t)batch * nq * hw * 4, cudaMemcpyDeviceToHost, st)))
+            return RFDETR_ERR_INFERENCE;
+    }
+    return RFB_CUDA_FAIL(cudaStreamSynchronize(st)) ? RFDETR_ERR_INFERENCE : RFDETR_OK;
+}
+
+// Run the forward for `batch` same-sized RGB images already packed at h_rgb.
+rfdetr_status forward_rgb_impl(rfdetr_context* ctx, const uint8_t* h_rgb, int batch, int w, int h) {
+    rfb::Engine& e = *ctx->engine;
+    const size_t bytes = (size_t)batch * w * h * 3;
+    rfdetr_status s = e.reserve(batch);
+    if (s != RFDETR_OK) return s;
+    s = e.reserve_rgb(bytes);
+    if (s != RFDETR_OK) return s;
+    if (RFB_CUDA_FAIL(cudaMemcpyAsync(e.d_rgb(), h_rgb, bytes, cudaMemcpyHostToDevice, e.stream())))
+        return RFDETR_ERR_INFERENCE;
+    s = e.enqueue(batch, e.d_rgb(), w, h);
+    if (s != RFDETR_OK) return s;
+    return e.finish();
+}
+
+void attach_names(const rfdetr_context* ctx, rfdetr_detection* d, size_t n) {
+    const auto& names = ctx->model->cfg.class_names;
+    for (size_t i = 0; i < n; ++i)
+        if (d[i].class_id < names.size()) d[i].class_name = names[d[i].class_id].c_str();
+}
+
+}  // namespace
+
+// ============================================================================
+// rfdetr.h
+// ============================================================================
+
+extern "C" rfdetr_context* rfdetr_init(const rfdetr_params* params, rfdetr_status* out_status) {
+    int device = 0;
+    if (const char* d = std::getenv("RFDETR_DEVICE")) device = std::atoi(d);
+    return init_impl(params, device, 1, out_status);
+}
+
+extern "C" void rfdetr_free(rfdetr_context* ctx) { delete ctx; }
+
+extern "C" const char* rfdetr_context_variant(const rfdetr_context* c) {
+    return (c && c->model) ? c->model->cfg.variant.c_str() : "";
+}
+extern "C" uint32_t rfdetr_context_image_size(const rfdetr_context* c) { return (c && c->model) ? c->model->cfg.image_size : 0; }
+extern "C" uint32_t rfdetr_context_num_queries(const rfdetr_context* c) { return (c && c->model) ? c->model->cfg.num_queries : 0; }
+extern "C" uint32_t rfdetr_context_num_classes(const rfdetr_context* c) { return (c && c->model) ? c->model->cfg.num_classes : 0; }
+extern "C" size_t rfdetr_context_n_tensors(const rfdetr_context* c) { return (c && c->model) ? c->n_tensors : 0; }
+
+extern "C" rfdetr_status rfdetr_detect(rfdetr_context* ctx, const rfdetr_image* img, const rfdetr_detect_params* params,
+                                       rfdetr_detection** out_detections, size_t* out_n) {
+    if (out_detections) *out_detections = nullptr;
+    if (out_n) *out_n = 0;
+    if (!ctx || !img || !params || !out_detections || !out_n) return RFDETR_ERR_INVALID_ARG;
+    if (!ctx->engine || img->width <= 0 || img->height <= 0 || img->rgb.empty()) return RFDETR_ERR_INVALID_ARG;
+    const size_t bytes = img->rgb.size();
+    if (!ctx->stage_in(bytes)) return RFDETR_ERR_OUT_OF_MEMORY;
+    std::memcpy(ctx->h_in, img->rgb.data(), bytes);
+    rfdetr_status s = forward_rgb_impl(ctx, ctx->h_in, 1, img->width, img->height);
+    if (s != RFDETR_OK) {
+        rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_detect: model forward failed");
+        return RFDETR_ERR_INFERENCE;
+    }
+    const rfb::Config& c = ctx->model->cfg;
+    const size_t nq = c.num_queries, nc = c.num_classes;
+    const int ms = ctx->engine->mask_side();
+    const size_t need = nq * nc + nq * 4 + (c.has_seg ? nq * (size_t)ms * ms : 0);
+    if (!ctx->stage_out(need)) return RFDETR_ERR_OUT_OF_MEMORY;
+    float* lg = ctx->h_out;
+    float* bx = lg + nq * nc;
+    float* mk = c.has_seg ? bx + nq * 4 : nullptr;
+    s = fetch_outputs(ctx, 1, lg, bx, mk);
+    if (s != RFDETR_OK) return RFDETR_ERR_INFERENCE;
+    rfb::select_detections(lg, bx, mk, ms, ms, nq, nc, params->threshold, params->top_k, params->class_filter,
+                           params->class_filter_len, img->width, img->height, out_detections, out_n);
+    if (*out_detections) attach_names(ctx, *out_detections, *out_n);
+    return RFDETR_OK;
+}
+
+// ============================================================================
+// rfdetr_b200.h
+// ============================================================================
+
+extern "C" rfdetr_context* rfdetr_b200_init(const rfdetr_params* params, const rfdetr_b200_params* b,
+                                            rfdetr_status* out_status) {
+    return init_impl(params, b ? b->device : 0, b && b->max_batch > 0 ? b->max_batch : 1, out_status);
+}
+
+extern "C" rfdetr_status rfdetr_b200_forward_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width,
+                                                 int height, float* out_logits, float* out_boxes, float* out_masks) {
+    if (!ctx || !ctx->engine || !rgb || batch <= 0 || width <= 0 || height <= 0) return RFDETR_ERR_INVALID_ARG;
+    rfdetr_status s = forward_rgb_impl(ctx, rgb, batch, width, height);
+    if (s != RFDETR_OK) return s;
+    return fetch_outputs(ctx, batch, out_logits, out_boxes, out_masks);
+}
+
+extern "C" rfdetr_status rfdetr_b200_forward_planar(rfdetr_context* ctx, const float* planar, int batch,
+                                                    float* out_logits, float* out_boxes, float* out_masks) {
+    if (!ctx || !ctx->engine || !planar || batch <= 0) return RFDETR_ERR_INVALID_ARG;
+    rfb::Engine& e = *ctx->engine;
+    rfdetr_status s = e.reserve(batch);
+    if (s != RFDETR_OK) return s;
+    const size_t S = e.cfg().image_size;
+    if (RFB_CUDA_FAIL(cudaMemcpyAsync(e.d_planar(), planar, (size_t)batch * 3 * S * S * 4, cudaMemcpyHostToDevice,
+                                      e.stream())))
+        return RFDETR_ERR_INFERENCE;
+    s = e.enqueue(batch, nullptr, 0, 0);
+    if (s == RFDETR_OK) s = e.finish();
+    if (s != RFDETR_OK) return s;
+    return fetch_outputs(ctx, batch, out_logits, out_boxes, out_masks);
+}
+
+extern "C" rfdetr_status rfdetr_b200_enqueue_device(rfdetr_context* ctx, const uint8_t* d_rgb, int batch, int width,
+                                                    int height) {
+    if (!ctx || !ctx->engine || !d_rgb || batch <= 0 || width <= 0 || height <= 0) return RFDETR_ERR_INVALID_ARG;
+    rfb::Engine& e = *ctx->engine;
+    rfdetr_status s = e.reserve(batch);
+    if (s != RFDETR_OK) return s;
+    return e.enqueue(batch, d_rgb, width, height);
+}
+
+extern "C" rfdetr_status rfdetr_b200_sync(rfdetr_context* ctx) {
+    if (!ctx || !ctx->engine) return RFDETR_ERR_INVALID_ARG;
+    return ctx->engine->finish();
+}
+
+extern "C" rfdetr_status rfdetr_b200_device_outputs(rfdetr_context* ctx, const float** l, const float** b,
+                                                    const float** m) {
+    if (!ctx || !ctx->engine) return RFDETR_ERR_INVALID_ARG;
+    if (l) *l = ctx->engine->logits();
+    if (b) *b = ctx->engine->boxes();
+    if (m) *m = ctx->model->cfg.has_seg ? ctx->engine->masks() : nullptr;
+    return RFDETR_OK;
+}
+
+extern "C" rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfdetr_image* const* imgs, size_t n,
+                                                  const rfdetr_detect_params* params, rfdetr_detection** out_dets,
+                                                  size_t* out_counts) {
+    if (!ctx || !ctx->engine || !imgs || !params || !out_dets || !out_counts) return RFDETR_ERR_INVALID_ARG;
+    for (size_t i = 0; i < n; ++i) { out_dets[i] = nullptr; out_counts[i] = 0; }
+    if (n == 0) return RFDETR_OK;
+    // Same-sized runs go through one batched forward; the preprocess kernel
+    // resizes each run to the model resolution on the GPU.
+    const rfb::Config& c = ctx->model->cfg;
+    const size_t nq = c.num_queries, nc = c.num_classes;
+    const int ms = ctx->engine->mask_side();
+    const size_t per = nq * nc + nq * 4 + (c.has_seg ? nq * (size_t)ms * ms : 0);
+    size_t i = 0;
+    while (i < n) {
+        if (!imgs[i] || imgs[i]->rgb.empty()) return RFDETR_ERR_INVALID_ARG;
+        const int w = imgs[i]->width, h = imgs[i]->height;
+        size_t j = i + 1;
+        while (j < n && imgs[j] && imgs[j]->width == w && imgs[j]->height == h) ++j;
+        const int batch = (int)(j - i);
+        const size_t img_bytes = (size_t)w * h * 3;
+        if (!ctx->stage_in(img_bytes * batch)) return RFDETR_ERR_OUT_OF_MEMORY;
+        for (size_t k = i; k < j; ++k) std::memcpy(ctx->h_in + (k - i) * img_bytes, imgs[k]->rgb.data(), img_bytes);
+        rfdetr_status s = forward_rgb_impl(ctx, ctx->h_in, batch, w, h);
+        if (s != RFDETR_OK) return RFDETR_ERR_INFERENCE;
+        if (!ctx->stage_out(per * batch)) return RFDETR_ERR_OUT_OF_MEMORY;
+        float* lg = ctx->h_out;
+        float* bx = lg + (size_t)batch * nq * nc;
+        float* mk = c.has_seg ? bx + (size_t)batch * nq * 4 : nullptr;
+        s = fetch_outputs(ctx, batch, lg, bx, mk);
+        if (s != RFDETR_OK) return s;
+        for (int k = 0; k < batch; ++k) {
+            rfb::select_detections(lg + (size_t)k * nq * nc, bx + (size_t)k * nq * 4,
+                                   mk ? mk + (size_t)k * nq * ms * ms : nullptr, ms, ms, nq, nc, params->threshold,
+                                   params->top_k, params->class_filter, params->class_filter_len, w, h,
+                                   &out_dets[i + k], &out_counts[i + k]);
+            if (out_dets[i + k]) attach_names(ctx, out_dets[i + k], out_counts[i + k]);
+        }
+        i = j;
+    }
+    return RFDETR_OK;
+}
+
+extern "C" int rfdetr_b200_device(const rfdetr_context* c) { return (c && c->engine) ? c->engine->device() : -1; }
+extern "C" int rfdetr_b200_mask_side(const rfdetr_context* c) { return (c && c->engine) ? c->engine->mask_side() : 0; }
+extern "C" int rfdetr_b200_kernels_per_forward(const rfdetr_context* c) {
+    return (c && c->engine) ? c->engine->kernels_per_forward() : 0;
+}
+extern "C" void* rfdetr_b200_stream(const rfdetr_context* c) { return (c && c->engine) ? (void*)c->engine->stream() : nullptr; }
+
+extern "C" long long rfdetr_b200_trace(rfdetr_context* ctx, const char* name, int batch, float* out, size_t cap) {
+    if (!ctx || !ctx->engine || !name || !out || batch <= 0 || batch > ctx->engine->max_batch()) return -1;
+    return ctx->engine->trace(name, batch, out, cap);
+}
+
+extern "C" rfdetr_status rfdetr_b200_inspect(const char* path, rfdetr_b200_model_info* out) {
+    if (!path || !out) return RFDETR_ERR_INVALID_ARG;
+    rfdetr_status st;
+    std::unique_ptr<rfb::Model> m(rfb::model_load(path, &st));
+    if (!m) return st;
+    st = rfb::model_validate(*m);
+    if (st != RFDETR_OK) return st;
+    st = rfb::engine_supports(m->cfg);
+    const rfb::Config& c = m->cfg;
+    std::memset(out, 0, sizeof(*out));
+    out->image_size = c.image_size;
+    out->patch_size = c.patch_size;
+    out->num_queries = c.num_queries;
+    out->num_classes = c.num_classes;
+    out->dim = c.backbone.dim;
+    out->depth = c.backbone.depth;
+    out->num_windows = c.backbone.num_windows;
+    out->dec_layers = c.decoder.layers;
+    out->has_segmentation_head = c.has_seg ? 1 : 0;
+    out->n_tensors = m->file.tensors.size();
+    std::strncpy(out->variant, c.variant.c_str(), sizeof(out->variant) - 1);
+    return st;
+}
+
+extern "C" int rfdetr_b200_dequantize(uint32_t type, const void* src, long long n, float* dst) {
+    if (!src || !dst || n < 0) return -1;
+    return rfb::dequantize(type, src, n, dst) ? 0 : -1;
+}
+
+// ============================================================================
+// rfdetr_capi.h
+// ============================================================================
+
+namespace {
+
+struct CapiHandle {
+    rfdetr_context* ctx = nullptr;
+    struct Det {
+        int class_id = 0;
+        std::string class_name;
+        float score = 0.f, x1 = 0, y1 = 0, x2 = 0, y2 = 0;
+        std::vector<uint8_t> mask_png;
+    };
+    std::vector<Det> last;
+    std::string last_json;
+};
+
+std::string make_json(int w, int h, const char* status, const rfdetr_detection* d, size_t n) {
+    std::ostringstream o;
+    o << "{\"status\":\"" << status << "\",\"image\":{\"width\":" << w << ",\"height\":" << h << "},\"detections\":[";
+    for (size_t i = 0; i < n; ++i) {
+        if (i) o << ",";
+        o << "{\"class_id\":" << d[i].class_id << ",\"score\":" << d[i].score << ",\"x1\":" << d[i].x1
+          << ",\"y1\":" << d[i].y1 << ",\"x2\":" << d[i].x2 << ",\"y2\":" << d[i].y2 << "}";
+    }
+    o << "]}";
+    return o.str();
+}
+
+char* dup_c(const std::string& s) {
+    char* b = static_cast<char*>(std::malloc(s.size() + 1));
+    if (!b) return nullptr;
+    std::memcpy(b, s.data(), s.size());
+    b[s.size()] = '\0';
+    return b;
+}
+
+int detect_common(rfdetr_handle_t handle, rfdetr_image* img, float threshold, uint32_t top_k, char** out_json) {
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    if (!h || !h->ctx || !img || !out_json) return -1;
+    *out_json = nullptr;
+    h->last.clear();
+    h->last_json.clear();
+    rfdetr_detect_params dp{};
+    dp.threshold = threshold;
+    dp.top_k = top_k;
+    rfdetr_detection* dets = nullptr;
+    size_t n = 0;
+    const rfdetr_status st = rfdetr_detect(h->ctx, img, &dp, &dets, &n);
+    const char* status = st == RFDETR_OK ? "ok" : (st == RFDETR_ERR_NOT_IMPLEMENTED ? "not_implemented" : rfdetr_status_str(st));
+    if (st == RFDETR_OK && dets) {
+        h->last.reserve(n);
+        for (size_t i = 0; i < n; ++i) {
+            CapiHandle::Det s;
+            s.class_id = (int)dets[i].class_id;
+            s.class_name = dets[i].class_name ? dets[i].class_name : "";
+            s.score = dets[i].score;
+            s.x1 = dets[i].x1; s.y1 = dets[i].y1; s.x2 = dets[i].x2; s.y2 = dets[i].y2;
+            if (dets[i].mask && dets[i].mask_width > 0 && dets[i].mask_height > 0)
+                rfdetr_encode_png(dets[i].mask, dets[i].mask_width, dets[i].mask_height, 1, s.mask_png);
+            h->last.push_back(std::move(s));
+        }
+    }
+    std::string json = make_json(rfdetr_image_width(img), rfdetr_image_height(img), status, dets, n);
+    rfdetr_detections_free(dets, n);
+    h->last_json = json;
+    *out_json = dup_c(json);
+    if (!*out_json) return (int)RFDETR_ERR_OUT_OF_MEMORY;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int rfdetr_capi_load(const char* model_path, int n_threads, rfdetr_handle_t* out_handle) {
+    if (!model_path || !out_handle) return -1;
+    *out_handle = 0;
+    rfdetr_params p{};
+    p.model_path = model_path;
+    p.n_threads = n_threads > 0 ? n_threads : 1;
+    rfdetr_status st;
+    rfdetr_context* ctx = rfdetr_init(&p, &st);
+    if (!ctx) return (int)st;
+    auto* h = new (std::nothrow) CapiHandle();
+    if (!h) {
+        rfdetr_free(ctx);
+        return (int)RFDETR_ERR_OUT_OF_MEMORY;
+    }
+    h->ctx = ctx;
+    *out_handle = reinterpret_cast<rfdetr_handle_t>(h);
+    return 0;
+}
+
+extern "C" int rfdetr_capi_unload(rfdetr_handle_t handle) {
+    if (handle == 0) return 0;
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    if (h->ctx) rfdetr_free(h->ctx);
+    delete h;
+    return 0;
+}
+
+extern "C" int rfdetr_capi_detect_path(rfdetr_handle_t handle, const char* path, float threshold, uint32_t top_k,
+                                       char** out_json) {
+    if (!handle || !path || !out_json) return -1;
+    *out_json = nullptr;
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    h->last.clear();
+    h->last_json.clear();
+    rfdetr_status st;
+    rfdetr_image* img = rfdetr_image_load_file(path, &st);
+    if (!img) return (int)st;
+    const int rc = detect_common(handle, img, threshold, top_k, out_json);
+    rfdetr_image_free(img);
+    return rc;
+}
+
+extern "C" int rfdetr_capi_detect_buffer(rfdetr_handle_t handle, const uint8_t* bytes, size_t len, float threshold,
+                                         uint32_t top_k, char** out_json) {
+    if (!handle || !bytes || len == 0 || !out_json) return -1;
+    *out_json = nullptr;
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    h->last.clear();
+    h->last_json.clear();
+    rfdetr_status st;
+    rfdetr_image* img = rfdetr_image_load_buffer(bytes, len, &st);
+    if (!img) return (int)st;
+    const int rc = detect_common(handle, img, threshold, top_k, out_json);
+    rfdetr_image_free(img);
+    return rc;
+}
+
+extern "C" void rfdetr_capi_free_string(char* s) { std::free(s); }
+
+extern "C" int rfdetr_capi_get_n_detections(rfdetr_handle_t handle) {
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    return h ? (int)h->last.size() : -1;
+}
+
+extern "C" int rfdetr_capi_get_detection_class_id(rfdetr_handle_t handle, int i) {
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    if (!h || i < 0 || (size_t)i >= h->last.size()) return -1;
+    return h->last[i].class_id;
+}
+
+extern "C" int rfdetr_capi_get_detection_box(rfdetr_handle_t handle, int i, float out_xyxy[4]) {
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    if (!h || i < 0 || (size_t)i >= h->last.size() || !out_xyxy) return -1;
+    const auto& d = h->last[i];
+    out_xyxy[0] = d.x1; out_xyxy[1] = d.y1; out_xyxy[2] = d.x2; out_xyxy[3] = d.y2;
+    return 0;
+}
+
+extern "C" float rfdetr_capi_get_detection_score(rfdetr_handle_t handle, int i) {
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    if (!h || i < 0 || (size_t)i >= h->last.size()) return -1.0f;
+    return h->last[i].score;
+}
+
+extern "C" int rfdetr_capi_get_detection_class_name(rfdetr_handle_t handle, int i, char* buf, int buf_size) {
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    if (!h || i < 0 || (size_t)i >= h->last.size()) return -1;
+    const std::string& s = h->last[i].class_name;
+    const int need = (int)s.size() + 1;
+    if (!buf || buf_size < need) return need;
+    std::memcpy(buf, s.data(), s.size());
+    buf[s.size()] = '\0';
+    return need;
+}
+
+extern "C" int rfdetr_capi_get_detection_mask_png(rfdetr_handle_t handle, int i, unsigned char* buf, int buf_size) {
+    auto* h = reinterpret_cast<CapiHandle*>(handle);
+    if (!h || i < 0 || (size_t)i >= h->last.size()) return -1;
+    const auto& mp = h->last[i].mask_png;
+    if (mp.empty()) return 0;
+    const int need = (int)mp.size();
+    if (!buf || buf_size < need) return need;
+    std::memcpy(buf, mp.data(), (size_t)need);
+    return need;
+}

@@ -1,0 +1,380 @@
+// Persistent, warp-specialized tcgen05 GEMM for sm_100a.
+//
+//   warp 0      TMA producer (one lane): A and B K-tiles -> smem ring
+//   warp 1      TMEM allocator; one lane issues tcgen05.mma (M=128, N=BN, K=16)
+//   warps 2..5  epilogue: tcgen05.ld accumulator rows, fused epilogue, store
+//
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the mainloop of tile i+1.  Tiles are assigned round-robin
+// over a grid of one CTA per SM, N-fastest so that CTAs running together share
+// the same A rows through L2 (A = activations, much larger than B = weights).
+// Every mbarrier wait is bounded; on timeout the CTA records an error word and
+// unwinds (no trap, no endless spin).
+#include "gemm.cuh"
+#include "sm100.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cstdio>
+#include <atomic>
+#include <mutex>
+
+namespace rfb {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+
+template <int BN>
+struct Cfg {
+    static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float act_fn(float v, int act) {
+    switch (act) {
+        case ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+        case ACT_RELU: return fmaxf(v, 0.0f);
+        case ACT_SILU: return v / (1.0f + expf(-v));
+        default: return v;
+    }
+}
+
+// Store 32 consecutive values of one row (columns n0..n0+31, masked by N).
+__device__ __forceinline__ void store_row_f32(float* dst, const float* v, int n0, int N) {
+    if (n0 + 32 <= N && (((uintptr_t)dst) & 15) == 0) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+        for (int j = 0; j < 32 && n0 + j < N; ++j) dst[j] = v[j];
+    }
+}
+
+__device__ __forceinline__ void store_row_f16(__half* dst, const float* v, int n0, int N) {
+    if (n0 + 32 <= N && (((uintptr_t)dst) & 15) == 0) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __half2 h0 = __floats2half2_rn(v[8 * j + 0], v[8 * j + 1]);
+            __half2 h1 = __floats2half2_rn(v[8 * j + 2], v[8 * j + 3]);
+            __half2 h2 = __floats2half2_rn(v[8 * j + 4], v[8 * j + 5]);
+            __half2 h3 = __floats2half2_rn(v[8 * j + 6], v[8 * j + 7]);
+            uint4 u;
+            u.x = *reinterpret_cast<uint32_t*>(&h0);
+            u.y = *reinterpret_cast<uint32_t*>(&h1);
+            u.z = *reinterpret_cast<uint32_t*>(&h2);
+            u.w = *reinterpret_cast<uint32_t*>(&h3);
+            d4[j] = u;
+        }
+    } else {
+        for (int j = 0; j < 32 && n0 + j < N; ++j) dst[j] = __float2half_rn(v[j]);
+    }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs p) {
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t* empty = full + C::STAGES;
+    uint64_t* tfull = empty + C::STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* cta_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int m_tiles = (p.M + BM - 1) / BM;
+    const int n_tiles = (p.N + BN - 1) / BN;
+    const int tiles_per_batch = m_tiles * n_tiles;
+    const int num_tiles = tiles_per_batch * p.batches;
+    const int num_kb = (p.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        *cta_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+    }
+    if (warp == 1) tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                const int b = tile / tiles_per_batch;
+                const int r = tile - b * tiles_per_batch;
+                const int mt = r / n_tiles, nt = r - mt * n_tiles;
+                const int arow = b * p.a_batch_rows + mt * BM;
+                const int brow = b * p.b_batch_rows + nt * BN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, cta_abort, p.err)) goto done;
+                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    tma_load_2d(&tmA, &full[stage], sA + stage * C::A_BYTES, kb * BK, arow);
+                    tma_load_2d(&tmB, &full[stage], sB + stage * C::B_BYTES, kb * BK, brow);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t IDESC = idesc_f16_f32(BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t acc_phase = (local >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, cta_abort, p.err)) goto done;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, cta_abort, p.err)) goto done;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        umma_f16(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), IDESC,
+                                 (kb | kk) != 0);
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                umma_commit(&tfull[acc]);
+            }
+        }
+    } else {
+        // ---------------- epilogue warps ----------------
+        const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
+        const int row_in_tile = quad * 32 + lane;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            const int b = tile / tiles_per_batch;
+            const int r = tile - b * tiles_per_batch;
+            const int mt = r / n_tiles, nt = r - mt * n_tiles;
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], acc_phase, cta_abort, p.err)) goto done;
+            tc_fence_after();
+            const int m = mt * BM + row_in_tile;
+            const bool row_ok = m < p.M;
+            const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+            const long long boff = (long long)b * p.out_batch_stride;
+            uint32_t raw[32];
+            float v[32];
+
+            if constexpr (EPI == EPI_LN) {
+                // BN == N: this thread owns the whole output row.
+                const float* rrow = p.resid ? p.resid + (size_t)m * p.ldr : nullptr;
+                float sum = 0.f;
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    tmem_ld32(tbase + c0, raw);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float x = __uint_as_float(raw[j]) + (p.bias ? p.bias[c0 + j] : 0.f);
+                        if (rrow && row_ok) x += rrow[c0 + j];
+                        sum += x;
+                    }
+                }
+                const float mean = sum / (float)BN;
+                float sq = 0.f;
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    tmem_ld32(tbase + c0, raw);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float x = __uint_as_float(raw[j]) + (p.bias ? p.bias[c0 + j] : 0.f);
+                        if (rrow && row_ok) x += rrow[c0 + j];
+                        const float d = x - mean;
+                        sq += d * d;
+                    }
+                }
+                const float rstd = 1.0f / sqrtf(sq / (float)BN + p.ln_eps);
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    tmem_ld32(tbase + c0, raw);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float x = __uint_as_float(raw[j]) + (p.bias ? p.bias[c0 + j] : 0.f);
+                        if (rrow && row_ok) x += rrow[c0 + j];
+                        x = (x - mean) * rstd * p.ln_g[c0 + j] + p.ln_b[c0 + j];
+                        v[j] = act_fn(x, p.act);
+                    }
+                    if (row_ok) {
+                        if (p.out32) store_row_f32(p.out32 + boff + (size_t)m * p.ld32 + c0, v, c0, p.N);
+                        if (p.out16) store_row_f16(p.out16 + boff + (size_t)m * p.ld16 + c0, v, c0, p.N);
+                    }
+                }
+            } else {
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    tmem_ld32(tbase + c0, raw);
+                    tmem_wait_ld();
+                    const int n0 = nt * BN + c0;
+                    if (!row_ok || n0 >= p.N) continue;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int n = n0 + j;
+                        const float bj = (p.bias && n < p.N) ? p.bias[n] : 0.f;
+                        v[j] = act_fn(__uint_as_float(raw[j]) + bj, p.act);
+                    }
+                    if constexpr (EPI == EPI_F16) {
+                        store_row_f16(p.out16 + boff + (size_t)m * p.ld16 + n0, v, n0, p.N);
+                    } else if constexpr (EPI == EPI_F32) {
+                        store_row_f32(p.out32 + boff + (size_t)m * p.ld32 + n0, v, n0, p.N);
+                    } else if constexpr (EPI == EPI_RESID) {
+                        float* dst = p.out32 + boff + (size_t)m * p.ld32 + n0;
+                        for (int j = 0; j < 32 && n0 + j < p.N; ++j) {
+                            const float s = p.colscale ? p.colscale[n0 + j] : 1.f;
+                            v[j] = dst[j] + s * v[j];
+                        }
+                        store_row_f32(dst, v, n0, p.N);
+                    } else if constexpr (EPI == EPI_PATCH) {
+                        const int img = m / p.patch_rows;
+                        const int rr = m - img * p.patch_rows;
+                        const int win = rr / p.patch_tp;
+                        const int tok = win * p.patch_t + 1 + (rr - win * p.patch_tp);
+                        const float* pos = p.posw + (size_t)tok * p.N + n0;
+                        for (int j = 0; j < 32 && n0 + j < p.N; ++j) v[j] += pos[j];
+                        store_row_f32(p.out32 + ((size_t)img * p.patch_ntok + tok) * p.ld32 + n0, v, n0, p.N);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+        }
+    }
+done:
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+int g_num_sms = 148;
+
+bool load_encode() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode != nullptr;
+}
+
+bool make_map(CUtensorMap* map, const void* base, int cols, long long rows, int ld, int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+cudaError_t launch(const GemmArgs& a, cudaStream_t st) {
+    static std::atomic<uint64_t> attr_set{0};  // per (BN, EPI) instantiation, one bit per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+        e = cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+        if (e != cudaSuccess) return e;
+        attr_set.fetch_or(bit);
+    }
+    CUtensorMap ta, tb;
+    const long long a_rows = (long long)a.a_batch_rows * (a.batches - 1) + a.M;
+    const long long b_rows = (long long)a.b_batch_rows * (a.batches - 1) + a.N;
+    if (!make_map(&ta, a.A, a.K, a_rows, a.lda, BM)) return cudaErrorInvalidValue;
+    if (!make_map(&tb, a.B, a.K, b_rows, a.ldb, BN)) return cudaErrorInvalidValue;
+    const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * a.batches;
+    const int grid = tiles < g_num_sms ? tiles : g_num_sms;
+    k_gemm<BN, EPI><<<grid, 192, Cfg<BN>::SMEM, st>>>(ta, tb, a);
+    return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t dispatch_bn(const GemmArgs& a, int bn, cudaStream_t st) {
+    switch (bn) {
+        case 256: return launch<256, EPI>(a, st);
+        case 128: return launch<128, EPI>(a, st);
+        default: return launch<64, EPI>(a, st);
+    }
+}
+
+}  // namespace
+
+void gemm_set_num_sms(int n) { g_num_sms = n > 0 ? n : 148; }
+
+cudaError_t gemm(const GemmArgs& a, cudaStream_t stream) {
+    if (!load_encode()) return cudaErrorNotSupported;
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.batches <= 0) return cudaErrorInvalidValue;
+    // TMA: 16-byte aligned base and row pitch
+    if ((a.lda % 8) || (a.ldb % 8) || (((uintptr_t)a.A) & 15) || (((uintptr_t)a.B) & 15)) return cudaErrorInvalidValue;
+    int bn;
+    if (a.epi == EPI_LN) {
+        if (a.N != 128 && a.N != 256) return cudaErrorInvalidValue;
+        if (!a.ln_g || !a.ln_b) return cudaErrorInvalidValue;
+        bn = a.N;
+    } else if (a.N % 256 == 0) {
+        bn = 256;
+    } else if (a.N > 64) {
+        bn = 128;
+    } else {
+        bn = 64;
+    }
+    switch (a.epi) {
+        case EPI_F16: return dispatch_bn<EPI_F16>(a, bn, stream);
+        case EPI_F32: return dispatch_bn<EPI_F32>(a, bn, stream);
+        case EPI_RESID: return dispatch_bn<EPI_RESID>(a, bn, stream);
+        case EPI_PATCH: return dispatch_bn<EPI_PATCH>(a, bn, stream);
+        case EPI_LN: return bn == 256 ? launch<256, EPI_LN>(a, stream) : launch<128, EPI_LN>(a, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace rfb

@@ -1,0 +1,63 @@
+// tcgen05 GEMM with fused epilogues: C = epilogue(A[M,K] . B[N,K]^T).
+// A (activations) and B (weights) are f16, K-contiguous; accumulation is f32
+// in TMEM.  See gemm.cu for the kernel design.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rfb {
+
+enum GemmEpi : int {
+    EPI_F16 = 0,    // out16 = act(acc + bias)
+    EPI_F32 = 1,    // out32 = act(acc + bias)
+    EPI_RESID = 2,  // out32 += colscale * act(acc + bias)        (layer-scale + residual)
+    EPI_PATCH = 3,  // patch embed: windowed row remap, + bias + windowed pos-embed -> out32
+    EPI_LN = 4,     // full-row LayerNorm(acc + bias [+ resid]) * g + b, act -> out32 / out16 (BN == N)
+};
+
+enum GemmAct : int { ACT_NONE = 0, ACT_GELU = 1, ACT_RELU = 2, ACT_SILU = 3 };
+
+struct GemmArgs {
+    // operands (row-major, K contiguous); lda/ldb in elements
+    const __half* A = nullptr;
+    int lda = 0;
+    const __half* B = nullptr;
+    int ldb = 0;
+    int M = 0, N = 0, K = 0;
+    // batching: batch b uses A rows [b*a_batch_rows, ...), B rows [b*b_batch_rows, ...)
+    int batches = 1;
+    int a_batch_rows = 0, b_batch_rows = 0;
+    long long out_batch_stride = 0;  // elements
+    // epilogue
+    int epi = EPI_F16;
+    int act = ACT_NONE;
+    const float* bias = nullptr;
+    const float* colscale = nullptr;
+    const float* ln_g = nullptr;
+    const float* ln_b = nullptr;
+    float ln_eps = 1e-5f;
+    const float* resid = nullptr;
+    int ldr = 0;
+    float* out32 = nullptr;
+    int ld32 = 0;
+    __half* out16 = nullptr;
+    int ld16 = 0;
+    // EPI_PATCH: rows are (image, window, patch-in-window) without CLS rows
+    int patch_tp = 0;      // patches per window
+    int patch_t = 0;       // tokens per window (patches + CLS)
+    int patch_rows = 0;    // patch rows per image
+    int patch_ntok = 0;    // tokens per image
+    const float* posw = nullptr;  // [ntok][N] windowed pos-embed
+    int* err = nullptr;    // device error word
+};
+
+// Launch on `stream`.  Picks the tile width from N (and requires BN == N for
+// EPI_LN).  Returns cudaSuccess or a launch / argument error.
+cudaError_t gemm(const GemmArgs& a, cudaStream_t stream);
+
+// Number of SMs used for the persistent grid (set once per device).
+void gemm_set_num_sms(int n);
+
+}  // namespace rfb

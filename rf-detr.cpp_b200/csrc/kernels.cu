@@ -1,0 +1,563 @@
+// Memory-bound kernels around the GEMMs: preprocessing, patch/conv im2col,
+// LayerNorm, backbone taps, two-stage box reparam, top-K selection, decoder
+// query setup, deformable sampling, segmentation resize / depthwise conv.
+// Each follows the arithmetic of the reference function cited beside it
+// (paths within localai-org/rf-detr.cpp).
+#include "kernels.cuh"
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace rfb {
+
+namespace {
+
+inline unsigned cdiv(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffff, v, o));
+    return v;
+}
+
+// ---- preprocess: src/image_io.cpp:207-248 ----------------------------------
+__global__ void k_preprocess(const uint8_t* __restrict__ rgb, int B, int w, int h, int S, float m0, float m1,
+                             float m2, float s0, float s1, float s2, float* __restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t total = (size_t)B * S * S;
+    if (i >= total) return;
+    const int b = (int)(i / ((size_t)S * S));
+    const int r = (int)(i - (size_t)b * S * S);
+    const int yy = r / S, xx = r - (r / S) * S;
+    const double scx = (double)w / (double)S, scy = (double)h / (double)S;
+    const double fy = ((double)yy + 0.5) * scy - 0.5;
+    const int y0r = (int)floor(fy);
+    const int y0 = min(max(y0r, 0), h - 1), y1 = min(max(y0r + 1, 0), h - 1);
+    const float wy = (float)(fy - (double)y0r);
+    const double fx = ((double)xx + 0.5) * scx - 0.5;
+    const int x0r = (int)floor(fx);
+    const int x0 = min(max(x0r, 0), w - 1), x1 = min(max(x0r + 1, 0), w - 1);
+    const float wx = (float)(fx - (double)x0r);
+    const uint8_t* img = rgb + (size_t)b * h * w * 3;
+    const float mean[3] = {m0, m1, m2}, sd[3] = {s0, s1, s2};
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const float p00 = (float)img[((size_t)y0 * w + x0) * 3 + c];
+        const float p01 = (float)img[((size_t)y0 * w + x1) * 3 + c];
+        const float p10 = (float)img[((size_t)y1 * w + x0) * 3 + c];
+        const float p11 = (float)img[((size_t)y1 * w + x1) * 3 + c];
+        const float top = p00 + (p01 - p00) * wx;
+        const float bot = p10 + (p11 - p10) * wx;
+        float v = (top + (bot - top) * wy) / 255.0f;
+        v = (v - mean[c]) / sd[c];
+        out[((size_t)b * 3 + c) * S * S + (size_t)yy * S + xx] = v;
+    }
+}
+
+// ---- patch im2col in windowed order: src/dinov2.cpp:339-408 -----------------
+__global__ void k_patch_im2col(const float* __restrict__ img, int B, int S, int p, int nw, int Kpad,
+                               __half* __restrict__ A) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int G = S / p, ws = G / nw, Tp = ws * ws;
+    const size_t rows = (size_t)B * nw * nw * Tp;
+    if (i >= rows * Kpad) return;
+    const size_t row = i / Kpad;
+    const int k = (int)(i - row * Kpad);
+    float v = 0.f;
+    if (k < 3 * p * p) {
+        const int b = (int)(row / ((size_t)nw * nw * Tp));
+        const int rr = (int)(row - (size_t)b * nw * nw * Tp);
+        const int win = rr / Tp, t = rr - win * Tp;
+        const int gy = (win / nw) * ws + t / ws, gx = (win % nw) * ws + t % ws;
+        const int c = k / (p * p), ky = (k / p) % p, kx = k % p;
+        v = img[((size_t)b * 3 + c) * S * S + (size_t)(gy * p + ky) * S + gx * p + kx];
+    }
+    A[i] = __float2half_rn(v);
+}
+
+__global__ void k_cls_rows(float* __restrict__ x, const float* __restrict__ clsrow, int B, int NW, int T, int D) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)B * NW * D) return;
+    const int d = (int)(i % D);
+    const size_t bw = i / D;
+    x[bw * T * D + d] = clsrow[d];
+}
+
+// ---- LayerNorm (ggml_norm then * g + b); warp per row, in-place safe -------
+template <int VPL>
+__global__ void k_layernorm(const float* x, int rows, int D, const float* __restrict__ g,
+                            const float* __restrict__ b, float eps, float* y32, __half* __restrict__ y16) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + (size_t)row * D;
+    float v[VPL];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = lane + 32 * i;
+        v[i] = c < D ? xr[c] : 0.f;
+        s += v[i];
+    }
+    const float mean = warp_sum(s) / (float)D;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = lane + 32 * i;
+        const float d = c < D ? v[i] - mean : 0.f;
+        q += d * d;
+    }
+    const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = lane + 32 * i;
+        if (c < D) {
+            const float o = (v[i] - mean) * rstd * g[c] + b[c];
+            if (y32) y32[(size_t)row * D + c] = o;
+            if (y16) y16[(size_t)row * D + c] = __float2half_rn(o);
+        }
+    }
+}
+
+// ---- backbone tap: src/dinov2.cpp:490-537 -----------------------------------
+__global__ void k_tap(const float* __restrict__ x, int B, int G, int nw, int D, const float* __restrict__ g,
+                      const float* __restrict__ bb, __half* __restrict__ taps, int ld, int col0) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // output pixel (b, gy, gx)
+    const int lane = threadIdx.x & 31;
+    if (row >= B * G * G) return;
+    const int b = row / (G * G), pix = row - b * G * G;
+    const int gy = pix / G, gx = pix - gy * G;
+    const int ws = G / nw, T = ws * ws + 1;
+    const int win = (gy / ws) * nw + gx / ws;
+    const int tok = win * T + 1 + (gy % ws) * ws + gx % ws;
+    const float* xr = x + ((size_t)b * nw * nw * T + tok) * D;
+    float v[12];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+        const int c = lane + 32 * i;
+        v[i] = c < D ? xr[c] : 0.f;
+        s += v[i];
+    }
+    const float mean = warp_sum(s) / (float)D;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+        const int c = lane + 32 * i;
+        const float d = c < D ? v[i] - mean : 0.f;
+        q += d * d;
+    }
+    const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)D + 1e-6f);
+    __half* o = taps + (size_t)row * ld + col0;
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+        const int c = lane + 32 * i;
+        if (c < D) o[c] = __float2half_rn((v[i] - mean) * rstd * g[c] + bb[c]);
+    }
+}
+
+// ---- 3x3 im2col (channels-last, 16-byte chunks) -----------------------------
+__global__ void k_im2col3x3(const __half* __restrict__ src, int lds, int B, int H, int W, int C,
+                            __half* __restrict__ A) {
+    const int chunks = C / 8;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t total = (size_t)B * H * W * 9 * chunks;
+    if (i >= total) return;
+    const int ch = (int)(i % chunks);
+    const int tap = (int)((i / chunks) % 9);
+    const size_t row = i / ((size_t)9 * chunks);
+    const int b = (int)(row / ((size_t)H * W));
+    const int pix = (int)(row - (size_t)b * H * W);
+    const int y = pix / W + tap / 3 - 1, x = pix % W + tap % 3 - 1;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (y >= 0 && y < H && x >= 0 && x < W)
+        v = *reinterpret_cast<const uint4*>(src + ((size_t)b * H * W + (size_t)y * W + x) * lds + ch * 8);
+    *reinterpret_cast<uint4*>(A + row * (size_t)(9 * C) + tap * C + ch * 8) = v;
+}
+
+// proposal of token (gy, gx) on a G x G grid, zeroed outside (0.01, 0.99):
+// src/two_stage.cpp:69-88
+__device__ __forceinline__ void proposal(int gy, int gx, int G, float (&p)[4]) {
+    const float fg = (float)G;
+    p[0] = ((float)gx + 0.5f) / fg;
+    p[1] = ((float)gy + 0.5f) / fg;
+    p[2] = 0.05f;
+    p[3] = 0.05f;
+    bool valid = true;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        if (!(p[c] > 0.01f && p[c] < 0.99f)) valid = false;
+    if (!valid) p[0] = p[1] = p[2] = p[3] = 0.f;
+}
+
+__global__ void k_mask_memory(const float* __restrict__ mem, int B, int G, int C, __half* __restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)B * G * G * C) return;
+    const int tok = (int)((i / C) % ((size_t)G * G));
+    float p[4];
+    proposal(tok / G, tok % G, G, p);
+    out[i] = __float2half_rn(p[2] > 0.f ? mem[i] : 0.f);
+}
+
+// src/two_stage.cpp:203-234
+__global__ void k_two_stage_boxes(const float* __restrict__ delta, int B, int G, float* __restrict__ bbox) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * G * G) return;
+    const int tok = i % (G * G);
+    float p[4];
+    proposal(tok / G, tok % G, G, p);
+    const float* d = delta + (size_t)i * 4;
+    float* o = bbox + (size_t)i * 4;
+    o[0] = d[0] * p[2] + p[0];
+    o[1] = d[1] * p[3] + p[1];
+    o[2] = expf(d[2]) * p[2];
+    o[3] = expf(d[3]) * p[3];
+}
+
+// ---- top-K: src/rfdetr_model.cpp:39-62 --------------------------------------
+constexpr int kTopkMax = 4096;
+
+__device__ __forceinline__ uint32_t float_order(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(1024) k_topk(const float* __restrict__ cls, int N, int NC, int K,
+                                                int32_t* __restrict__ idx) {
+    __shared__ unsigned long long keys[kTopkMax];
+    const int b = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    int P = 1;
+    while (P < N) P <<= 1;
+    for (int t = warp; t < P; t += nwarps) {
+        unsigned long long key = ~0ull;
+        if (t < N) {
+            const float* r = cls + ((size_t)b * N + t) * NC;
+            float m = -INFINITY;
+            for (int c = lane; c < NC; c += 32) m = fmaxf(m, r[c]);
+            m = warp_max(m);
+            key = ((unsigned long long)(~float_order(m)) << 32) | (unsigned)t;
+        }
+        if (lane == 0) keys[t] = key;
+    }
+    __syncthreads();
+    // bitonic sort ascending (smaller key = higher score, then lower index)
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = keys[i], c = keys[ixj];
+                    const bool up = (i & k) == 0;
+                    if ((a > c) == up) {
+                        keys[i] = c;
+                        keys[ixj] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int q = threadIdx.x; q < K; q += blockDim.x) idx[(size_t)b * K + q] = (int32_t)(keys[q] & 0xffffffffu);
+}
+
+// ---- decoder inputs: src/rfdetr_model.cpp:233-271, src/decoder.cpp:383-417 ---
+__global__ void k_query_init(const float* __restrict__ bbox_all, const int32_t* __restrict__ idx,
+                             const float* __restrict__ lrn, const float* __restrict__ feat, int N, int NQ, int Dm,
+                             float* __restrict__ refp, __half* __restrict__ sine, float* __restrict__ tgt,
+                             __half* __restrict__ tgt16) {
+    const int bq = blockIdx.x;  // b*NQ + q
+    const int b = bq / NQ, q = bq - b * NQ;
+    const int t = idx[bq];
+    const float* box = bbox_all + ((size_t)b * N + t) * 4;
+    const float* l = lrn + (size_t)q * 4;
+    float rp[4];
+    rp[0] = l[0] * box[2] + box[0];
+    rp[1] = l[1] * box[3] + box[1];
+    rp[2] = expf(l[2]) * box[2];
+    rp[3] = expf(l[3]) * box[3];
+    if (threadIdx.x < 4) refp[(size_t)bq * 4 + threadIdx.x] = rp[threadIdx.x];
+    const int half = Dm / 2;
+    const int comp[4] = {1, 0, 2, 3};
+    for (int j = threadIdx.x; j < 2 * Dm; j += blockDim.x) {
+        const int c = j / half, kk = j - c * half;
+        const float v = rp[comp[c]] * 6.28318530717958647692f;
+        const float inv = expf(-logf(10000.0f) * (float)((kk / 2) * 2) / (float)half);
+        const float arg = v * inv;
+        sine[(size_t)bq * 2 * Dm + j] = __float2half_rn((kk & 1) ? cosf(arg) : sinf(arg));
+    }
+    for (int d = threadIdx.x; d < Dm; d += blockDim.x) {
+        const float f = feat[(size_t)q * Dm + d];
+        tgt[(size_t)bq * Dm + d] = f;
+        tgt16[(size_t)bq * Dm + d] = __float2half_rn(f);
+    }
+}
+
+__global__ void k_add_to_f16(const float* __restrict__ a, const float* __restrict__ b, size_t n,
+                             __half* __restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __float2half_rn(a[i] + b[i]);
+}
+
+__global__ void k_to_f16(const float* __restrict__ a, size_t n, __half* __restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __float2half_rn(a[i]);
+}
+
+// ---- deformable sampling: src/decoder.cpp:127-207, 236-285 ------------------
+// One warp per query; each lane owns 8 consecutive channels (16 bytes of f16
+// value per corner), 2 lanes per 16-channel head.
+__global__ void k_deform(const __half* __restrict__ value, const float* __restrict__ so_aw, int ld_soaw,
+                         const float* __restrict__ refp, int B, int NQ, int G, int H, int P, int Dm,
+                         __half* __restrict__ out) {
+    const int bq = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (bq >= B * NQ) return;
+    const int b = bq / NQ;
+    const int hd = Dm / H;
+    const float* row = so_aw + (size_t)bq * ld_soaw;
+    const float* rp = refp + (size_t)bq * 4;
+    const float r0 = rp[0], r1 = rp[1], r2 = rp[2], r3 = rp[3];
+    const float off_scale = 0.5f / (float)P;
+    const __half* vb = value + (size_t)b * G * G * Dm;
+    for (int c = lane; c < Dm / 8; c += 32) {
+        const int h = (c * 8) / hd;
+        // softmax over the P attention logits of head h (ggml_soft_max)
+        float mx = -INFINITY;
+        for (int p = 0; p < P; ++p) mx = fmaxf(mx, row[H * P * 2 + h * P + p]);
+        float sum = 0.f;
+        for (int p = 0; p < P; ++p) sum += expf(row[H * P * 2 + h * P + p] - mx);
+        const float inv = 1.0f / sum;
+        float acc[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+        for (int p = 0; p < P; ++p) {
+            const float wa = expf(row[H * P * 2 + h * P + p] - mx) * inv;
+            const float sx = (row[(h * P + p) * 2 + 0] * off_scale) * r2 + r0;
+            const float sy = (row[(h * P + p) * 2 + 1] * off_scale) * r3 + r1;
+            const float ix = sx * (float)G - 0.5f, iy = sy * (float)G - 0.5f;
+            const int ix0 = (int)floorf(ix), iy0 = (int)floorf(iy);
+            const float wx1 = ix - (float)ix0, wy1 = iy - (float)iy0;
+            const float wx0 = 1.f - wx1, wy0 = 1.f - wy1;
+            float s[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s[e] = 0.f;
+#pragma unroll
+            for (int corner = 0; corner < 4; ++corner) {
+                const int xi = ix0 + (corner & 1), yi = iy0 + (corner >> 1);
+                if (xi < 0 || xi >= G || yi < 0 || yi >= G) continue;
+                const float wgt = ((corner & 1) ? wx1 : wx0) * ((corner >> 1) ? wy1 : wy0);
+                const uint4 u = *reinterpret_cast<const uint4*>(vb + ((size_t)yi * G + xi) * Dm + c * 8);
+                const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(h2[e]);
+                    s[2 * e] += wgt * f.x;
+                    s[2 * e + 1] += wgt * f.y;
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] += wa * s[e];
+        }
+        uint4 o;
+        __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) oh[e] = __floats2half2_rn(acc[2 * e], acc[2 * e + 1]);
+        *reinterpret_cast<uint4*>(out + (size_t)bq * Dm + c * 8) = o;
+    }
+}
+
+// src/rfdetr_model.cpp:438-448
+__global__ void k_box_reparam(const float* __restrict__ d, const float* __restrict__ r, int n, float* __restrict__ o) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float* dd = d + (size_t)i * 4;
+    const float* rr = r + (size_t)i * 4;
+    float* oo = o + (size_t)i * 4;
+    oo[0] = dd[0] * rr[2] + rr[0];
+    oo[1] = dd[1] * rr[3] + rr[1];
+    oo[2] = expf(dd[2]) * rr[2];
+    oo[3] = expf(dd[3]) * rr[3];
+}
+
+// ---- segmentation: src/segmentation.cpp:187-199 (ggml_interpolate bilinear) --
+__global__ void k_resize_bilinear(const float* __restrict__ src, int B, int G, int T, int C, float* __restrict__ dst) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)B * T * T * C) return;
+    const int c = (int)(i % C);
+    const size_t pix = i / C;
+    const int b = (int)(pix / ((size_t)T * T));
+    const int r = (int)(pix - (size_t)b * T * T);
+    const int yy = r / T, xx = r - (r / T) * T;
+    const float sf = (float)T / (float)G;
+    const float fy = ((float)yy + 0.5f) / sf - 0.5f;
+    int y0 = (int)floorf(fy), y1 = y0 + 1;
+    y0 = min(max(y0, 0), G - 1);
+    y1 = min(max(y1, 0), G - 1);
+    const float dy = fminf(fmaxf(fy - (float)y0, 0.f), 1.f);
+    const float fx = ((float)xx + 0.5f) / sf - 0.5f;
+    int x0 = (int)floorf(fx), x1 = x0 + 1;
+    x0 = min(max(x0, 0), G - 1);
+    x1 = min(max(x1, 0), G - 1);
+    const float dx = fminf(fmaxf(fx - (float)x0, 0.f), 1.f);
+    const float* s = src + (size_t)b * G * G * C + c;
+    const float a = s[((size_t)y0 * G + x0) * C], bb = s[((size_t)y0 * G + x1) * C];
+    const float cc = s[((size_t)y1 * G + x0) * C], d = s[((size_t)y1 * G + x1) * C];
+    dst[i] = a * (1 - dx) * (1 - dy) + bb * dx * (1 - dy) + cc * (1 - dx) * dy + d * dx * dy;
+}
+
+// depthwise 3x3 + bias + channel LN (src/segmentation.cpp:68-92); warp per pixel
+__global__ void k_dwconv_ln(const float* __restrict__ x, int B, int H, int W, int C, const float* __restrict__ w9,
+                            const float* __restrict__ bias, const float* __restrict__ g, const float* __restrict__ bb,
+                            float eps, __half* __restrict__ out) {
+    const int pix = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (pix >= B * H * W) return;
+    const int b = pix / (H * W), r = pix - b * H * W;
+    const int y = r / W, xq = r - (r / W) * W;
+    float v[8];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int c = lane + 32 * i;
+        float acc = 0.f;
+        if (c < C) {
+#pragma unroll
+            for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx) {
+                    const int sy = y + ky - 1, sx = xq + kx - 1;
+                    if (sy < 0 || sy >= H || sx < 0 || sx >= W) continue;
+                    acc += w9[c * 9 + ky * 3 + kx] * x[(((size_t)b * H + sy) * W + sx) * C + c];
+                }
+            acc += bias[c];
+        }
+        v[i] = acc;
+        s += c < C ? acc : 0.f;
+    }
+    const float mean = warp_sum(s) / (float)C;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int c = lane + 32 * i;
+        const float d = c < C ? v[i] - mean : 0.f;
+        q += d * d;
+    }
+    const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)C + eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int c = lane + 32 * i;
+        if (c < C) out[(size_t)pix * C + c] = __float2half_rn((v[i] - mean) * rstd * g[c] + bb[c]);
+    }
+}
+
+}  // namespace
+
+cudaError_t preprocess_u8(const uint8_t* rgb, int B, int w, int h, int S, const float* mean3, const float* std3,
+                          float* out, cudaStream_t st) {
+    const size_t n = (size_t)B * S * S;
+    k_preprocess<<<cdiv(n, 256), 256, 0, st>>>(rgb, B, w, h, S, mean3[0], mean3[1], mean3[2], std3[0], std3[1],
+                                               std3[2], out);
+    return cudaGetLastError();
+}
+
+cudaError_t patch_im2col(const float* img, int B, int S, int p, int nw, int Kpad, __half* A, cudaStream_t st) {
+    const int G = S / p, Tp = (G / nw) * (G / nw);
+    const size_t n = (size_t)B * nw * nw * Tp * Kpad;
+    k_patch_im2col<<<cdiv(n, 256), 256, 0, st>>>(img, B, S, p, nw, Kpad, A);
+    return cudaGetLastError();
+}
+
+cudaError_t write_cls_rows(float* x, const float* clsrow, int B, int NW, int T, int D, cudaStream_t st) {
+    const size_t n = (size_t)B * NW * D;
+    k_cls_rows<<<cdiv(n, 256), 256, 0, st>>>(x, clsrow, B, NW, T, D);
+    return cudaGetLastError();
+}
+
+cudaError_t layernorm(const float* x, int rows, int D, const float* g, const float* b, float eps, float* y32,
+                      __half* y16, cudaStream_t st) {
+    if (D > 512) return cudaErrorInvalidValue;
+    const unsigned blocks = cdiv(rows, 8);
+    if (D <= 256) k_layernorm<8><<<blocks, 256, 0, st>>>(x, rows, D, g, b, eps, y32, y16);
+    else k_layernorm<16><<<blocks, 256, 0, st>>>(x, rows, D, g, b, eps, y32, y16);
+    return cudaGetLastError();
+}
+
+cudaError_t backbone_tap(const float* x, int B, int G, int nw, int D, const float* g, const float* b, __half* taps,
+                         int ld, int col0, cudaStream_t st) {
+    if (D > 384) return cudaErrorInvalidValue;
+    k_tap<<<cdiv((size_t)B * G * G, 8), 256, 0, st>>>(x, B, G, nw, D, g, b, taps, ld, col0);
+    return cudaGetLastError();
+}
+
+cudaError_t im2col3x3(const __half* src, int lds, int B, int H, int W, int C, __half* A, cudaStream_t st) {
+    if (C % 8 || lds % 8) return cudaErrorInvalidValue;
+    const size_t n = (size_t)B * H * W * 9 * (C / 8);
+    k_im2col3x3<<<cdiv(n, 256), 256, 0, st>>>(src, lds, B, H, W, C, A);
+    return cudaGetLastError();
+}
+
+cudaError_t mask_memory(const float* mem, int B, int G, int C, __half* out, cudaStream_t st) {
+    const size_t n = (size_t)B * G * G * C;
+    k_mask_memory<<<cdiv(n, 256), 256, 0, st>>>(mem, B, G, C, out);
+    return cudaGetLastError();
+}
+
+cudaError_t two_stage_boxes(const float* delta, int B, int G, float* bbox, cudaStream_t st) {
+    k_two_stage_boxes<<<cdiv((size_t)B * G * G, 256), 256, 0, st>>>(delta, B, G, bbox);
+    return cudaGetLastError();
+}
+
+cudaError_t topk_tokens(const float* cls, int B, int N, int NC, int K, int32_t* idx, cudaStream_t st) {
+    if (N > kTopkMax || K > N) return cudaErrorInvalidValue;
+    k_topk<<<B, 1024, 0, st>>>(cls, N, NC, K, idx);
+    return cudaGetLastError();
+}
+
+cudaError_t query_init(const float* bbox_all, const int32_t* idx, const float* lrn_rp, const float* feat, int B,
+                       int N, int NQ, int Dm, float* refp, __half* sine, float* tgt, __half* tgt16, cudaStream_t st) {
+    k_query_init<<<B * NQ, 256, 0, st>>>(bbox_all, idx, lrn_rp, feat, N, NQ, Dm, refp, sine, tgt, tgt16);
+    return cudaGetLastError();
+}
+
+cudaError_t add_to_f16(const float* a, const float* b, size_t n, __half* out, cudaStream_t st) {
+    k_add_to_f16<<<cdiv(n, 256), 256, 0, st>>>(a, b, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t to_f16(const float* a, size_t n, __half* out, cudaStream_t st) {
+    k_to_f16<<<cdiv(n, 256), 256, 0, st>>>(a, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t deform_sample(const __half* value, const float* so_aw, int ld_soaw, const float* refp, int B, int NQ,
+                          int G, int heads, int points, int Dm, __half* out, cudaStream_t st) {
+    if (Dm % 8 || (Dm / heads) % 8) return cudaErrorInvalidValue;
+    k_deform<<<cdiv((size_t)B * NQ, 4), 128, 0, st>>>(value, so_aw, ld_soaw, refp, B, NQ, G, heads, points, Dm, out);
+    return cudaGetLastError();
+}
+
+cudaError_t box_reparam(const float* delta, const float* refp, int n, float* out, cudaStream_t st) {
+    k_box_reparam<<<cdiv(n, 256), 256, 0, st>>>(delta, refp, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t resize_bilinear(const float* src, int B, int G, int T, int C, float* dst, cudaStream_t st) {
+    const size_t n = (size_t)B * T * T * C;
+    k_resize_bilinear<<<cdiv(n, 256), 256, 0, st>>>(src, B, G, T, C, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t dwconv_ln(const float* x, int B, int H, int W, int C, const float* w9, const float* bias,
+                      const float* g, const float* b, float eps, __half* out, cudaStream_t st) {
+    if (C > 256) return cudaErrorInvalidValue;
+    k_dwconv_ln<<<cdiv((size_t)B * H * W, 8), 256, 0, st>>>(x, B, H, W, C, w9, bias, g, b, eps, out);
+    return cudaGetLastError();
+}
+
+}  // namespace rfb

@@ -1,0 +1,42 @@
+// Operator entry points of rfdetr_b200.h: thin C wrappers over the kernels.
+#include "rfdetr_b200.h"
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+extern "C" int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int epi,
+                                   int act, const float* bias, const float* colscale, const float* ln_g,
+                                   const float* ln_b, float ln_eps, const float* resid, int ldr, float* out32,
+                                   int ld32, void* out16, int ld16, void* stream) {
+    if (epi != rfb::EPI_F16 && epi != rfb::EPI_F32 && epi != rfb::EPI_RESID && epi != rfb::EPI_LN)
+        return (int)cudaErrorInvalidValue;
+    if ((epi == rfb::EPI_F16 && !out16) || ((epi == rfb::EPI_F32 || epi == rfb::EPI_RESID) && !out32))
+        return (int)cudaErrorInvalidValue;
+    rfb::GemmArgs a;
+    a.A = static_cast<const __half*>(A);
+    a.lda = lda;
+    a.B = static_cast<const __half*>(B);
+    a.ldb = ldb;
+    a.M = M; a.N = N; a.K = K;
+    a.epi = epi; a.act = act;
+    a.bias = bias; a.colscale = colscale;
+    a.ln_g = ln_g; a.ln_b = ln_b; a.ln_eps = ln_eps;
+    a.resid = resid; a.ldr = ldr;
+    a.out32 = out32; a.ld32 = ld32;
+    a.out16 = static_cast<__half*>(out16); a.ld16 = ld16;
+    return (int)rfb::gemm(a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int rfdetr_b200_op_attention(const void* q, const void* k, const void* v, int ldq, int ldk, int ldv,
+                                        void* o, int ldo, int seq_len, int groups, int heads, int head_dim,
+                                        float scale, void* stream) {
+    return (int)rfb::attention(static_cast<const __half*>(q), static_cast<const __half*>(k),
+                               static_cast<const __half*>(v), ldq, ldk, ldv, static_cast<__half*>(o), ldo, seq_len,
+                               groups, heads, head_dim, scale, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int rfdetr_b200_op_deform(const void* value, const float* so_aw, int ld_soaw, const float* refp, int batch,
+                                     int nq, int grid, int heads, int points, int dm, void* out, void* stream) {
+    return (int)rfb::deform_sample(static_cast<const __half*>(value), so_aw, ld_soaw, refp, batch, nq, grid, heads,
+                                   points, dm, static_cast<__half*>(out), static_cast<cudaStream_t>(stream));
+}

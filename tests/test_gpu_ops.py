@@ -1,0 +1,142 @@
+"""Kernel-level numerics on the B200: each sm_100a operator of librfdetr.so,
+called through its C-ABI entry point, against a plain PyTorch fp32 (float64
+accumulate) reference of the same op.  Inputs are f16 (what the kernels
+consume); the tolerance covers f16 output rounding and f32 accumulation order.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _lib():
+    from rfdetr_b200 import lib
+    return lib.lib()
+
+
+def _p(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def rel(a, b):
+    a = a.double().cpu()
+    b = b.double().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+GEMM_SHAPES = [(300, 256, 256), (1000, 1152, 384), (517, 91, 256), (200, 4, 256), (4097, 1536, 384),
+               (333, 384, 1536), (129, 256, 592), (64, 512, 512), (2000, 2048, 256), (1, 128, 64)]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+@pytest.mark.parametrize("epi,act", [(0, 0), (1, 0), (0, 1), (0, 2), (2, 0)])
+def test_gemm(M, N, K, epi, act):
+    torch.manual_seed(M * 7 + N + K)
+    dev = "cuda:0"
+    lda = (K + 7) // 8 * 8
+    A = torch.zeros(M, lda, dtype=torch.float16, device=dev)
+    A[:, :K] = torch.randn(M, K, device=dev).half()
+    B = torch.zeros(N, lda, dtype=torch.float16, device=dev)
+    B[:, :K] = (torch.randn(N, K, device=dev) * 0.05).half()
+    bias = torch.randn(N, device=dev) * 0.1
+    scale = torch.rand(N, device=dev) + 0.5
+    ref = A[:, :K].double() @ B[:, :K].double().T + bias.double()
+    if act == 1:
+        ref = F.gelu(ref)
+    elif act == 2:
+        ref = F.relu(ref)
+    out16 = torch.zeros(M, N, dtype=torch.float16, device=dev) if epi == 0 else None
+    out32 = torch.randn(M, N, device=dev) if epi in (1, 2) else None
+    base = out32.clone() if epi == 2 else None
+    rc = _lib().rfdetr_b200_op_gemm(_p(A), lda, _p(B), lda, M, N, K, epi, act, _p(bias),
+                                    _p(scale) if epi == 2 else None, None, None, 0.0, None, 0,
+                                    _p(out32), N, _p(out16), N, _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    if epi == 0:
+        assert rel(out16, ref) < 2e-3
+    elif epi == 1:
+        assert rel(out32, ref) < 1e-4
+    else:
+        assert rel(out32, base.double() + scale.double() * ref) < 1e-4
+
+
+@pytest.mark.parametrize("N", [128, 256])
+@pytest.mark.parametrize("act,with_resid", [(0, True), (3, False)])
+def test_gemm_layernorm_epilogue(N, act, with_resid):
+    torch.manual_seed(N + act)
+    dev = "cuda:0"
+    M, K = 777, 640
+    A = torch.randn(M, K, device=dev).half()
+    B = (torch.randn(N, K, device=dev) * 0.05).half()
+    bias = torch.randn(N, device=dev) * 0.1
+    g = torch.rand(N, device=dev) + 0.5
+    b = torch.randn(N, device=dev) * 0.1
+    resid = torch.randn(M, N, device=dev) if with_resid else None
+    v = A.double() @ B.double().T + bias.double()
+    if with_resid:
+        v = v + resid.double()
+    ref = F.layer_norm(v, (N,), g.double(), b.double(), 1e-5)
+    if act == 3:
+        ref = F.silu(ref)
+    out32 = torch.zeros(M, N, device=dev)
+    out16 = torch.zeros(M, N, dtype=torch.float16, device=dev)
+    rc = _lib().rfdetr_b200_op_gemm(_p(A), K, _p(B), K, M, N, K, 4, act, _p(bias), None, _p(g), _p(b), 1e-5,
+                                    _p(resid), N if with_resid else 0, _p(out32), N, _p(out16), N, _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert rel(out32, ref) < 1e-4
+    assert rel(out16, ref) < 2e-3
+
+
+@pytest.mark.parametrize("L,groups,heads,hd", [(101, 8, 6, 64), (580, 2, 6, 64), (1616, 1, 6, 64),
+                                               (300, 3, 8, 32), (17, 5, 6, 64), (64, 2, 8, 32)])
+def test_attention(L, groups, heads, hd):
+    torch.manual_seed(L + groups)
+    dev = "cuda:0"
+    D = heads * hd
+    qkv = torch.randn(groups * L, 3 * D, device=dev).half()
+    o = torch.zeros(groups * L, D, dtype=torch.float16, device=dev)
+    scale = 1.0 / math.sqrt(hd)
+    rc = _lib().rfdetr_b200_op_attention(_p(qkv), _p(qkv[:, D:]), _p(qkv[:, 2 * D:]), 3 * D, 3 * D, 3 * D, _p(o), D,
+                                         L, groups, heads, hd, scale, _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    x = qkv.double().view(groups, L, 3, heads, hd)
+    q, k, v = x[:, :, 0].transpose(1, 2), x[:, :, 1].transpose(1, 2), x[:, :, 2].transpose(1, 2)
+    ref = torch.softmax(q @ k.transpose(-1, -2) * scale, -1) @ v
+    ref = ref.transpose(1, 2).reshape(groups * L, D)
+    assert rel(o, ref) < 4e-3
+
+
+def test_deform_matches_grid_sample():
+    torch.manual_seed(0)
+    dev = "cuda:0"
+    B, G, NQ, H, P, Dm = 2, 12, 37, 16, 2, 256
+    value = torch.randn(B * G * G, Dm, device=dev).half()
+    so_aw = torch.randn(B * NQ, H * P * 3, device=dev)
+    refp = torch.cat([torch.rand(B * NQ, 2, device=dev), torch.rand(B * NQ, 2, device=dev) * 0.5 + 0.05], 1)
+    out = torch.zeros(B * NQ, Dm, dtype=torch.float16, device=dev)
+    rc = _lib().rfdetr_b200_op_deform(_p(value), _p(so_aw), H * P * 3, _p(refp), B, NQ, G, H, P, Dm, _p(out),
+                                      _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    so = so_aw[:, :H * P * 2].double().view(B, NQ, H, P, 2)
+    aw = torch.softmax(so_aw[:, H * P * 2:].double().view(B, NQ, H, P), -1)
+    rp = refp.double().view(B, NQ, 1, 1, 4)
+    loc = rp[..., :2] + so / P * rp[..., 2:] * 0.5
+    hd = Dm // H
+    vmap = value.double().view(B, G, G, H, hd).permute(0, 3, 4, 1, 2).reshape(B * H, hd, G, G)
+    grid = (2 * loc - 1).permute(0, 2, 1, 3, 4).reshape(B * H, NQ, P, 2)
+    s = F.grid_sample(vmap, grid, mode="bilinear", padding_mode="zeros", align_corners=False)  # (B*H, hd, NQ, P)
+    s = (s * aw.permute(0, 2, 1, 3).reshape(B * H, 1, NQ, P)).sum(-1)
+    ref = s.view(B, H, hd, NQ).permute(0, 3, 1, 2).reshape(B * NQ, Dm)
+    assert rel(out, ref) < 2e-3
