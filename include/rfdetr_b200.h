@@ -72,6 +72,14 @@ void* rfdetr_b200_stream(const rfdetr_context* ctx);              /* the context
  * Returns the element count, or -1 (unknown name / capacity too small). */
 long long rfdetr_b200_trace(rfdetr_context* ctx, const char* name, int batch, float* out, size_t cap);
 
+/* Per-launch timing of the forward pass.  rfdetr_b200_profile_enable(ctx, 1)
+ * makes subsequent forwards record a CUDA event after every kernel launch;
+ * after the forward has completed, rfdetr_b200_profile_read fills up to `cap`
+ * entries (launch name, NUL-terminated, at names + i*name_len; duration in
+ * ms) and returns the number of launches of that forward. */
+void rfdetr_b200_profile_enable(rfdetr_context* ctx, int on);
+int  rfdetr_b200_profile_read(rfdetr_context* ctx, char* names, int name_len, float* ms, int cap);
+
 /* Host-only inspection of a GGUF file (no GPU needed), for loaders and tests:
  * parses, validates the tensor inventory (src/model_loader.cpp:212-750) and
  * checks that the engine implements the configuration. */

@@ -293,6 +293,23 @@ extern "C" long long rfdetr_b200_trace(rfdetr_context* ctx, const char* name, in
     return ctx->engine->trace(name, batch, out, cap);
 }
 
+extern "C" void rfdetr_b200_profile_enable(rfdetr_context* ctx, int on) {
+    if (ctx && ctx->engine) ctx->engine->set_profiling(on != 0);
+}
+
+extern "C" int rfdetr_b200_profile_read(rfdetr_context* ctx, char* names, int name_len, float* ms, int cap) {
+    if (!ctx || !ctx->engine) return -1;
+    const auto prof = ctx->engine->profile();
+    for (int i = 0; i < (int)prof.size() && i < cap; ++i) {
+        if (names && name_len > 0) {
+            std::strncpy(names + (size_t)i * name_len, prof[i].first.c_str(), (size_t)name_len - 1);
+            names[(size_t)i * name_len + name_len - 1] = '\0';
+        }
+        if (ms) ms[i] = prof[i].second;
+    }
+    return (int)prof.size();
+}
+
 extern "C" rfdetr_status rfdetr_b200_inspect(const char* path, rfdetr_b200_model_info* out) {
     if (!path || !out) return RFDETR_ERR_INVALID_ARG;
     rfdetr_status st;

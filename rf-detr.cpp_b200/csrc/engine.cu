@@ -31,6 +31,7 @@ Engine::~Engine() {
     if (rgb_u8_) cudaFree(rgb_u8_);
     for (void* p : wallocs_) cudaFree(p);
     if (d_err_) cudaFree(d_err_);
+    for (cudaEvent_t e : prof_ev_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -465,12 +466,29 @@ struct Launcher {
     int* err;
     int count = 0;
     bool ok = true;
+    // optional per-launch events (profiling)
+    std::vector<cudaEvent_t>* ev = nullptr;
+    std::vector<std::string>* names = nullptr;
+    int* used = nullptr;
+    void mark(const char* what) {
+        if (!ev) return;
+        if (*used >= (int)ev->size()) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return;
+            ev->push_back(e);
+            names->emplace_back();
+        }
+        cudaEventRecord((*ev)[*used], st);
+        (*names)[*used] = what;
+        ++*used;
+    }
     void check(cudaError_t e, const char* what) {
         ++count;
         if (e != cudaSuccess && ok) {
             rfdetr_logf(RFDETR_LOG_ERROR, "forward: %s failed: %s", what, cudaGetErrorString(e));
             ok = false;
         }
+        mark(what);
     }
     void gemm(const char* what, const __half* A, int lda, int M, const DLin& W, int epi, int act, float* out32,
               int ld32, __half* out16, int ld16, const float* colscale = nullptr, const DNorm* ln = nullptr,
@@ -493,6 +511,13 @@ rfdetr_status Engine::enqueue(int B, const uint8_t* src_rgb, int src_w, int src_
     if (B <= 0 || B > max_batch_) return RFDETR_ERR_INVALID_ARG;
     if (RFB_CUDA_FAIL(cudaSetDevice(device_))) return RFDETR_ERR_INFERENCE;
     Launcher L{stream_, d_err_};
+    if (profiling_) {
+        L.ev = &prof_ev_;
+        L.names = &prof_names_;
+        L.used = &prof_used_;
+        prof_used_ = 0;
+        L.mark("start");
+    }
     cudaStream_t st = stream_;
     const int D = D_, G = G_, Dm = Dm_, NQ = NQ_;
     const int Mb = B * Ntok_, Mp = B * G * G, Mq = B * NQ;
@@ -633,6 +658,16 @@ rfdetr_status Engine::enqueue(int B, const uint8_t* src_rgb, int src_w, int src_
     }
     launches_ = L.count;
     return L.ok ? RFDETR_OK : RFDETR_ERR_INFERENCE;
+}
+
+std::vector<std::pair<std::string, float>> Engine::profile() {
+    std::vector<std::pair<std::string, float>> out;
+    for (int i = 1; i < prof_used_; ++i) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, prof_ev_[i - 1], prof_ev_[i]) != cudaSuccess) ms = -1.f;
+        out.emplace_back(prof_names_[i], ms);
+    }
+    return out;
 }
 
 rfdetr_status Engine::finish() {

@@ -12,6 +12,7 @@
 
 #include <memory>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace rfb {
@@ -68,6 +69,12 @@ public:
     // Number of kernels one forward launches (for the benchmark record).
     int kernels_per_forward() const { return launches_; }
 
+    // Per-launch timing: when enabled, the next forwards record a CUDA event
+    // after every launch on the engine stream; profile() returns
+    // (name, milliseconds) of each launch of the last forward (after finish()).
+    void set_profiling(bool on) { profiling_ = on; }
+    std::vector<std::pair<std::string, float>> profile();
+
 private:
     Engine() = default;
     rfdetr_status upload_weights(const Model& m);
@@ -79,6 +86,10 @@ private:
     cudaStream_t stream_ = nullptr;
     int max_batch_ = 0;
     int launches_ = 0;
+    bool profiling_ = false;
+    std::vector<cudaEvent_t> prof_ev_;
+    std::vector<std::string> prof_names_;
+    int prof_used_ = 0;
 
     // dims
     int S_ = 0, P_ = 0, G_ = 0, nw_ = 0, ws_ = 0, Tp_ = 0, T_ = 0, NW_ = 0, Ntok_ = 0;

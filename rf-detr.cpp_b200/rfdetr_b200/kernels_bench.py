@@ -1,0 +1,80 @@
+"""Micro-benchmark of single engine operators at model shapes.
+
+    python -m rfdetr_b200.kernels_bench gemm --m 51712 --n 1536 --k 384 [--epi 0 --act 1]
+    python -m rfdetr_b200.kernels_bench attn --seq 1616 --groups 32 --heads 6 --hd 64
+
+Times `--iters` launches with CUDA events on the current stream (after
+`--warmup` launches) and prints one JSON line: ms per launch and achieved
+TFLOP/s (algorithmic FLOPs: 2*M*N*K for a GEMM, 4*L^2*hd per (group, head)
+for attention).  Used for ncu captures of one kernel in isolation.
+"""
+import argparse
+import json
+import math
+
+import torch
+
+from . import lib
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("op", choices=["gemm", "attn"])
+    ap.add_argument("--m", type=int, default=51712)
+    ap.add_argument("--n", type=int, default=1536)
+    ap.add_argument("--k", type=int, default=384)
+    ap.add_argument("--epi", type=int, default=0)
+    ap.add_argument("--act", type=int, default=1)
+    ap.add_argument("--seq", type=int, default=1616)
+    ap.add_argument("--groups", type=int, default=32)
+    ap.add_argument("--heads", type=int, default=6)
+    ap.add_argument("--hd", type=int, default=64)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args()
+    L = lib.lib()
+    dev = "cuda:0"
+    st = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device=dev).manual_seed(0)
+    if a.op == "gemm":
+        A = torch.randn(a.m, a.k, device=dev, generator=g).half()
+        B = (torch.randn(a.n, a.k, device=dev, generator=g) * 0.05).half()
+        bias = torch.zeros(a.n, device=dev)
+        out16 = torch.empty(a.m, a.n, dtype=torch.float16, device=dev)
+        out32 = torch.empty(a.m, a.n, device=dev) if a.epi in (1, 2) else None
+
+        def run():
+            rc = L.rfdetr_b200_op_gemm(A.data_ptr(), a.k, B.data_ptr(), a.k, a.m, a.n, a.k, a.epi, a.act,
+                                       bias.data_ptr(), None, None, None, 0.0, None, 0,
+                                       out32.data_ptr() if out32 is not None else None, a.n, out16.data_ptr(),
+                                       a.n, st)
+            assert rc == 0, rc
+        flops = 2.0 * a.m * a.n * a.k
+        name = f"gemm M={a.m} N={a.n} K={a.k} epi={a.epi} act={a.act}"
+    else:
+        D = a.heads * a.hd
+        qkv = torch.randn(a.groups * a.seq, 3 * D, device=dev, generator=g).half()
+        o = torch.empty(a.groups * a.seq, D, dtype=torch.float16, device=dev)
+
+        def run():
+            rc = L.rfdetr_b200_op_attention(qkv.data_ptr(), qkv[:, D:].data_ptr(), qkv[:, 2 * D:].data_ptr(),
+                                            3 * D, 3 * D, 3 * D, o.data_ptr(), D, a.seq, a.groups, a.heads, a.hd,
+                                            1.0 / math.sqrt(a.hd), st)
+            assert rc == 0, rc
+        flops = 4.0 * a.seq * a.seq * a.hd * a.groups * a.heads
+        name = f"attention L={a.seq} groups={a.groups} heads={a.heads} hd={a.hd}"
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.iters
+    print(json.dumps({"op": name, "ms": round(ms, 5), "tflops": round(flops / ms / 1e9, 1)}))
+
+
+if __name__ == "__main__":
+    main()

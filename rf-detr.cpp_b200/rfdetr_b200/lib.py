@@ -103,6 +103,8 @@ SIGNATURES = {
     "rfdetr_b200_kernels_per_forward": (C.c_int, [C.c_void_p]),
     "rfdetr_b200_stream": (C.c_void_p, [C.c_void_p]),
     "rfdetr_b200_trace": (C.c_longlong, [C.c_void_p, C.c_char_p, C.c_int, C.c_void_p, C.c_size_t]),
+    "rfdetr_b200_profile_enable": (None, [C.c_void_p, C.c_int]),
+    "rfdetr_b200_profile_read": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int, C.c_void_p, C.c_int]),
     "rfdetr_b200_inspect": (C.c_int, [C.c_char_p, C.POINTER(ModelInfo)]),
     "rfdetr_b200_dequantize": (C.c_int, [C.c_uint32, C.c_void_p, C.c_longlong, C.c_void_p]),
     "rfdetr_b200_op_gemm": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -205,6 +207,27 @@ class Engine:
         if n < 0:
             raise KeyError(name)
         return out[:n].copy()
+
+    def enqueue_device(self, d_rgb_ptr: int, batch: int, width: int, height: int):
+        check(lib().rfdetr_b200_enqueue_device(self._ctx, C.c_void_p(d_rgb_ptr), batch, width, height),
+              "enqueue_device")
+
+    def sync(self):
+        check(lib().rfdetr_b200_sync(self._ctx), "sync")
+
+    def profile_enable(self, on: bool = True):
+        lib().rfdetr_b200_profile_enable(self._ctx, 1 if on else 0)
+
+    def profile_read(self, cap: int = 4096, name_len: int = 48):
+        names = C.create_string_buffer(cap * name_len)
+        ms = np.zeros(cap, np.float32)
+        n = lib().rfdetr_b200_profile_read(self._ctx, names, name_len, _ptr(ms), cap)
+        raw = names.raw
+        out = []
+        for i in range(min(n, cap)):
+            nm = raw[i * name_len:(i + 1) * name_len].split(b"\0", 1)[0].decode()
+            out.append((nm, float(ms[i])))
+        return out
 
     def kernels_per_forward(self) -> int:
         return lib().rfdetr_b200_kernels_per_forward(self._ctx)

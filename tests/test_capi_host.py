@@ -1,0 +1,206 @@
+"""Host-side checks of librfdetr.so that need no GPU: the library loads and
+exports every symbol the headers declare; the GGUF loader's contract and
+error codes (reference tests/test_model_loader.cpp, src/model_loader.cpp:
+212-371, 703-750); the block dequantizers against gguf-py; image decoding;
+and the flat C API's invalid-handle behaviour (tests/test_capi_flat.cpp,
+tests/test_capi_accessors.cpp)."""
+import ctypes as C
+import os
+import re
+import struct
+import zlib
+
+import numpy as np
+import pytest
+
+from rfdetr_b200 import lib, synth
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in ("rfdetr.h", "rfdetr_capi.h", "rfdetr_b200.h"):
+        src = open(os.path.join(REPO, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"\b(rfdetr_[a-z0-9_]+)\s*\(", src):
+            names.add(m.group(1))
+    names.discard("rfdetr_log_cb")
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    L = lib.lib()
+    syms = declared_symbols()
+    assert len(syms) >= 45
+    for s in sorted(syms):
+        assert hasattr(L, s), s
+    assert syms <= set(lib.SIGNATURES), sorted(syms - set(lib.SIGNATURES))
+
+
+def test_status_strings():
+    L = lib.lib()
+    assert L.rfdetr_status_str(0) == b"ok"
+    assert L.rfdetr_status_str(-7) == b"model load error"
+    assert L.rfdetr_status_str(-99) == b"not implemented"
+    assert L.rfdetr_status_str(12345) == b"unknown error"
+
+
+@pytest.mark.parametrize("variant", ["tiny", "seg-tiny", "base", "grid52"])
+def test_inspect_valid(variant, make_model):
+    path = make_model(variant, "f16", 0)
+    st, info = lib.inspect(path)
+    cfg = synth.get_variant(variant)
+    assert st == 0
+    assert info.image_size == cfg["image_size"] and info.num_queries == cfg["num_queries"]
+    assert info.num_windows == cfg["backbone"]["num_windows"]
+    assert info.has_segmentation_head == int(cfg["segmentation_head"])
+    assert info.n_tensors == len(synth.tensor_specs(cfg))
+    assert info.variant.decode() == variant
+
+
+def _write(tmp_path, name, variant="tiny", drop=None, meta_override=None, dtype="f32"):
+    cfg = synth.get_variant(variant)
+    st = synth.make_state(cfg, 0)
+    if drop:
+        st.pop(drop)
+    if meta_override:
+        cfg.update(meta_override)
+    p = str(tmp_path / name)
+    synth.write_gguf(p, variant, cfg, st, dtype)
+    return p
+
+
+def test_inspect_errors(tmp_path):
+    assert lib.inspect(str(tmp_path / "nope.gguf"))[0] == -2
+    p = _write(tmp_path, "missing.gguf", drop="decoder.layers.1.norm3.bias")
+    assert lib.inspect(p)[0] == -7  # missing tensor -> RFDETR_ERR_MODEL_LOAD
+    p = _write(tmp_path, "seg_missing.gguf", variant="seg-tiny", drop="segmentation_head.blocks.1.dwconv.weight")
+    assert lib.inspect(p)[0] == -7
+    good = _write(tmp_path, "good.gguf")
+    data = open(good, "rb").read()
+    (tmp_path / "trunc.gguf").write_bytes(data[: len(data) // 2])
+    assert lib.inspect(str(tmp_path / "trunc.gguf"))[0] == -6
+    (tmp_path / "garbage.gguf").write_bytes(b"NOTAGGUF" + bytes(64))
+    assert lib.inspect(str(tmp_path / "garbage.gguf"))[0] == -6
+    p = _write(tmp_path, "mode.gguf", meta_override={"resize_mode": "bogus"})
+    assert lib.inspect(p)[0] == -6
+
+
+def test_inspect_rejects_unsupported_config(tmp_path):
+    cfg = synth.get_variant("tiny")
+    cfg["backbone"]["heads"] = 8  # head_dim 48: not implemented by the kernels
+    p = str(tmp_path / "h8.gguf")
+    synth.write_gguf(p, "tiny", cfg, synth.make_state(synth.get_variant("tiny"), 0), "f32")
+    assert lib.inspect(p)[0] == -6
+
+
+@pytest.mark.parametrize("qt", ["F16", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "BF16"])
+def test_dequantizers_match_gguf_py(qt):
+    import gguf
+    T = gguf.GGMLQuantizationType[qt]
+    a = (np.random.default_rng(1).standard_normal((8, 512)) * 0.05).astype(np.float32)
+    if qt == "F16":
+        raw = a.astype(np.float16).view(np.uint8)
+    else:
+        raw = gguf.quants.quantize(a, T)
+    ours = lib.dequantize(int(T), raw, a.size)
+    ref = gguf.quants.dequantize(raw, T).reshape(-1)
+    assert np.array_equal(ours, ref.astype(np.float32))
+
+
+@pytest.mark.parametrize("qt", ["Q4_K", "Q5_K", "Q6_K"])
+def test_kquant_dequantizers_match_gguf_py(qt):
+    import gguf
+    T = gguf.GGMLQuantizationType[qt]
+    bs = {"Q4_K": 144, "Q5_K": 176, "Q6_K": 210}[qt]
+    rng = np.random.default_rng(2)
+    raw = rng.integers(0, 256, (16, bs), dtype=np.uint8)
+    # keep the f16 scales finite and small
+    for off in ((0, 2) if qt != "Q6_K" else (208,)):
+        raw[:, off:off + 2] = np.frombuffer(
+            (rng.uniform(-0.01, 0.01, 16).astype(np.float16)).tobytes(), np.uint8).reshape(16, 2)
+    ours = lib.dequantize(int(T), raw, 16 * 256)
+    ref = gguf.quants.dequantize(raw, T).reshape(-1).astype(np.float32)
+    assert np.allclose(ours, ref, rtol=0, atol=0)
+
+
+def _png(rgb, color_type=2, filt=0):
+    h, w = rgb.shape[:2]
+    rows = b"".join(bytes([filt]) + rgb[y].tobytes() for y in range(h))
+    if filt == 1:  # Sub filter for 3-channel
+        out = bytearray()
+        for y in range(h):
+            r = rgb[y].reshape(-1).astype(np.int32)
+            sub = (r - np.concatenate([np.zeros(3, np.int32), r[:-3]])) & 0xFF
+            out += bytes([1]) + sub.astype(np.uint8).tobytes()
+        rows = bytes(out)
+
+    def chunk(t, d):
+        return struct.pack(">I", len(d)) + t + d + struct.pack(">I", zlib.crc32(t + d) & 0xFFFFFFFF)
+    return (b"\x89PNG\r\n\x1a\n" + chunk(b"IHDR", struct.pack(">IIBBBBB", w, h, 8, color_type, 0, 0, 0)) +
+            chunk(b"IDAT", zlib.compress(rows)) + chunk(b"IEND", b""))
+
+
+@pytest.mark.parametrize("filt", [0, 1])
+def test_png_and_ppm_decode(filt):
+    L = lib.lib()
+    rgb = np.random.default_rng(4).integers(0, 256, (17, 23, 3), dtype=np.uint8)
+    for blob in (_png(rgb, filt=filt), b"P6\n23 17\n255\n" + rgb.tobytes()):
+        st = C.c_int(0)
+        img = L.rfdetr_image_load_buffer(blob, len(blob), C.byref(st))
+        assert img and st.value == 0
+        assert L.rfdetr_image_width(img) == 23 and L.rfdetr_image_height(img) == 17
+        data = np.ctypeslib.as_array(L.rfdetr_image_rgb_data(img), shape=(17 * 23 * 3,))
+        assert np.array_equal(data.reshape(17, 23, 3), rgb)
+        L.rfdetr_image_free(img)
+    st = C.c_int(0)
+    assert not L.rfdetr_image_load_buffer(b"\x00\x01garbage", 9, C.byref(st))
+    assert st.value == -5
+    assert not L.rfdetr_image_load_file(b"/nonexistent/x.png", C.byref(st))
+    assert st.value == -2
+
+
+def test_image_from_rgb_copies():
+    L = lib.lib()
+    rgb = np.arange(4 * 5 * 3, dtype=np.uint8).reshape(4, 5, 3)
+    st = C.c_int(0)
+    img = L.rfdetr_image_from_rgb_buffer(rgb.ctypes.data, 5, 4, C.byref(st))
+    rgb[:] = 0
+    data = np.ctypeslib.as_array(L.rfdetr_image_rgb_data(img), shape=(60,))
+    assert data[5] == 5
+    L.rfdetr_image_free(img)
+    assert not L.rfdetr_image_from_rgb_buffer(None, 5, 4, C.byref(st)) and st.value == -1
+
+
+def test_flat_capi_invalid_handles():
+    L = lib.lib()
+    assert L.rfdetr_capi_unload(0) == 0
+    assert L.rfdetr_capi_get_n_detections(0) == -1
+    assert L.rfdetr_capi_get_detection_class_id(0, 0) == -1
+    xy = (C.c_float * 4)()
+    assert L.rfdetr_capi_get_detection_box(0, 0, xy) == -1
+    assert L.rfdetr_capi_get_detection_score(0, 0) == -1.0
+    assert L.rfdetr_capi_get_detection_class_name(0, 0, None, 0) == -1
+    assert L.rfdetr_capi_get_detection_mask_png(0, 0, None, 0) == -1
+    out = C.c_void_p()
+    assert L.rfdetr_capi_detect_path(0, b"x.png", 0.5, 10, C.byref(out)) == -1
+    h = C.c_size_t(0)
+    assert L.rfdetr_capi_load(None, 1, C.byref(h)) == -1
+    assert L.rfdetr_capi_load(b"/nonexistent.gguf", 1, C.byref(h)) == -2 and h.value == 0
+
+
+def test_init_errors_without_touching_the_gpu(tmp_path):
+    L = lib.lib()
+    st = C.c_int(0)
+    p = lib.Params(None, 1, lib.LOG_CB(), None)
+    assert not L.rfdetr_init(C.byref(p), C.byref(st)) and st.value == -1
+    p = lib.Params(b"/nonexistent.gguf", 1, lib.LOG_CB(), None)
+    assert not L.rfdetr_init(C.byref(p), C.byref(st)) and st.value == -2
+    bad = _write(tmp_path, "missing.gguf", drop="heads.class_embed.bias")
+    msgs = []
+    cb = lib.LOG_CB(lambda lvl, msg, ud: msgs.append(msg.decode()))
+    p = lib.Params(bad.encode(), 1, cb, None)
+    assert not L.rfdetr_init(C.byref(p), C.byref(st)) and st.value == -7
+    assert any("missing tensor" in m for m in msgs)
+    L.rfdetr_set_log_callback(lib.LOG_CB(), None)
