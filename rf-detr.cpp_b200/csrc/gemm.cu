@@ -16,6 +16,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cstdio>
+#include <cstring>
 #include <atomic>
 #include <mutex>
 
@@ -33,7 +34,8 @@ struct Cfg {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int OUT_STAGE = 4 * 8192;  // per epilogue warp: 2 x (32 rows x 128 B)
+    static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ float act_fn(float v, int act) {
@@ -77,15 +79,28 @@ __device__ __forceinline__ void store_row_f16(__half* dst, const float* v, int n
     }
 }
 
+// Swizzled (128-byte pattern) staging of one 32-row x 128-byte box: thread
+// `lane` owns row `lane`; 16-byte chunk j lands at chunk (j ^ (lane & 7)).
+__device__ __forceinline__ uint32_t swz(uint32_t base, int lane, int j) {
+    return base + lane * 128 + ((j ^ (lane & 7)) << 4);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
-k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs p) {
+k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+       const __grid_constant__ CUtensorMap tmO16, const __grid_constant__ CUtensorMap tmO32, const GemmArgs p) {
     using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint8_t* out_stage = smem + C::STAGES * C::STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(out_stage + C::OUT_STAGE);
     uint64_t* empty = full + C::STAGES;
     uint64_t* tfull = empty + C::STAGES;
     uint64_t* tempty = tfull + 2;
@@ -179,6 +194,8 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         // ---------------- epilogue warps ----------------
         const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
         const int row_in_tile = quad * 32 + lane;
+        const uint32_t wbuf = smem_u32(out_stage + quad * 8192);
+        int sc = 0;  // staging-buffer toggle (double buffering across chunks)
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int b = tile / tiles_per_batch;
@@ -189,6 +206,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
             if (!mbar_wait(&tfull[acc], acc_phase, cta_abort, p.err)) goto done;
             tc_fence_after();
             const int m = mt * BM + row_in_tile;
+            const int m0w = mt * BM + quad * 32;
             const bool row_ok = m < p.M;
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
             const long long boff = (long long)b * p.out_batch_stride;
@@ -233,9 +251,102 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         x = (x - mean) * rstd * p.ln_g[c0 + j] + p.ln_b[c0 + j];
                         v[j] = act_fn(x, p.act);
                     }
-                    if (row_ok) {
+                    if (p.tma_out) {
+                        // f32 box [32 rows][32 cols] at wbuf, f16 box [32 rows][64 cols] at wbuf + 4096
+                        const int half = (c0 >> 5) & 1;
+                        if (lane == 0) bulk_wait_read<0>();
+                        __syncwarp();
+                        if (p.out32) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                st_shared_v4(swz(wbuf, lane, j), __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                                             __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+                        }
+                        if (p.out16) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                st_shared_v4(swz(wbuf + 4096, lane, j + 4 * half), pack_half2(v[8 * j], v[8 * j + 1]),
+                                             pack_half2(v[8 * j + 2], v[8 * j + 3]), pack_half2(v[8 * j + 4], v[8 * j + 5]),
+                                             pack_half2(v[8 * j + 6], v[8 * j + 7]));
+                        }
+                        fence_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            if (p.out32) tma_store_3d(&tmO32, out_stage + quad * 8192, c0, m0w, b);
+                            if (p.out16 && (half == 1 || c0 + 32 >= BN))
+                                tma_store_3d(&tmO16, out_stage + quad * 8192 + 4096, c0 & ~63, m0w, b);
+                            bulk_commit();
+                        }
+                    } else if (row_ok) {
                         if (p.out32) store_row_f32(p.out32 + boff + (size_t)m * p.ld32 + c0, v, c0, p.N);
                         if (p.out16) store_row_f16(p.out16 + boff + (size_t)m * p.ld16 + c0, v, c0, p.N);
+                    }
+                }
+            } else if (EPI != EPI_PATCH && p.tma_out) {
+                if constexpr (EPI == EPI_F16) {
+                    // 64-column chunks: one 128-byte f16 box row per thread
+                    for (int c0 = 0; c0 < BN; c0 += 64) {
+                        uint32_t raw2[32];
+                        tmem_ld32(tbase + c0, raw);
+                        tmem_ld32(tbase + c0 + 32, raw2);
+                        tmem_wait_ld();
+                        const int n0 = nt * BN + c0;
+                        const uint32_t buf = wbuf + (sc & 1) * 4096;
+                        if (lane == 0) bulk_wait_read<1>();
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            float w8[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const int jj = 8 * j + e;
+                                const int n = n0 + jj;
+                                const float bj = (p.bias && n < p.N) ? p.bias[n] : 0.f;
+                                const uint32_t rv = jj < 32 ? raw[jj] : raw2[jj - 32];
+                                w8[e] = act_fn(__uint_as_float(rv) + bj, p.act);
+                            }
+                            st_shared_v4(swz(buf, lane, j), pack_half2(w8[0], w8[1]), pack_half2(w8[2], w8[3]),
+                                         pack_half2(w8[4], w8[5]), pack_half2(w8[6], w8[7]));
+                        }
+                        fence_async_smem();
+                        __syncwarp();
+                        if (lane == 0 && n0 < p.N) {
+                            tma_store_3d(&tmO16, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
+                            bulk_commit();
+                        }
+                        ++sc;
+                    }
+                } else {
+                    // f32 (store or residual reduce-add): 32-column chunks
+                    for (int c0 = 0; c0 < BN; c0 += 32) {
+                        tmem_ld32(tbase + c0, raw);
+                        tmem_wait_ld();
+                        const int n0 = nt * BN + c0;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int n = n0 + j;
+                            const float bj = (p.bias && n < p.N) ? p.bias[n] : 0.f;
+                            float x = act_fn(__uint_as_float(raw[j]) + bj, p.act);
+                            if (EPI == EPI_RESID && p.colscale) x *= (n < p.N ? p.colscale[n] : 0.f);
+                            v[j] = x;
+                        }
+                        const uint32_t buf = wbuf + (sc & 1) * 4096;
+                        if (lane == 0) bulk_wait_read<1>();
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            st_shared_v4(swz(buf, lane, j), __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                                         __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+                        fence_async_smem();
+                        __syncwarp();
+                        if (lane == 0 && n0 < p.N) {
+                            if (EPI == EPI_RESID)
+                                tma_reduce_add_3d(&tmO32, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
+                            else
+                                tma_store_3d(&tmO32, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
+                            bulk_commit();
+                        }
+                        ++sc;
                     }
                 }
             } else {
@@ -275,6 +386,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
         }
+        if (lane == 0) bulk_wait<0>();
     }
 done:
     __syncthreads();
@@ -314,8 +426,26 @@ bool make_map(CUtensorMap* map, const void* base, int cols, long long rows, int 
     return r == CUDA_SUCCESS;
 }
 
+// 3-D output map (cols, rows, batch) with a 128-byte swizzled box of 32 rows.
+bool make_out_map(CUtensorMap* map, const void* base, bool f16, int cols, int rows, int batches, int ld,
+                  long long batch_stride) {
+    const int esz = f16 ? 2 : 4;
+    if (!base || ((uintptr_t)base & 15) || ((size_t)ld * esz) % 16) return false;
+    if (batches > 1 && ((size_t)batch_stride * esz) % 16) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batches};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * esz,
+                             (cuuint64_t)(batches > 1 ? batch_stride : (long long)ld * rows) * esz};
+    cuuint32_t box[3] = {(cuuint32_t)(128 / esz), 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return g_encode(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int EPI>
-cudaError_t launch(const GemmArgs& a, cudaStream_t st) {
+cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
+    GemmArgs a = a_in;
     static std::atomic<uint64_t> attr_set{0};  // per (BN, EPI) instantiation, one bit per device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -331,9 +461,16 @@ cudaError_t launch(const GemmArgs& a, cudaStream_t st) {
     const long long b_rows = (long long)a.b_batch_rows * (a.batches - 1) + a.N;
     if (!make_map(&ta, a.A, a.K, a_rows, a.lda, BM)) return cudaErrorInvalidValue;
     if (!make_map(&tb, a.B, a.K, b_rows, a.ldb, BN)) return cudaErrorInvalidValue;
+    CUtensorMap to16, to32;
+    std::memset(&to16, 0, sizeof(to16));
+    std::memset(&to32, 0, sizeof(to32));
+    bool tma = EPI != EPI_PATCH;
+    if (tma && a.out16) tma = make_out_map(&to16, a.out16, true, a.N, a.M, a.batches, a.ld16, a.out_batch_stride);
+    if (tma && a.out32) tma = make_out_map(&to32, a.out32, false, a.N, a.M, a.batches, a.ld32, a.out_batch_stride);
+    a.tma_out = tma ? 1 : 0;
     const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * a.batches;
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-    k_gemm<BN, EPI><<<grid, 192, Cfg<BN>::SMEM, st>>>(ta, tb, a);
+    k_gemm<BN, EPI><<<grid, 192, Cfg<BN>::SMEM, st>>>(ta, tb, to16, to32, a);
     return cudaGetLastError();
 }
 

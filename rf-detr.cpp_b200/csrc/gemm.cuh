@@ -51,6 +51,7 @@ struct GemmArgs {
     int patch_ntok = 0;    // tokens per image
     const float* posw = nullptr;  // [ntok][N] windowed pos-embed
     int* err = nullptr;    // device error word
+    int tma_out = 0;       // set by the launcher: outputs written through TMA stores
 };
 
 // Launch on `stream`.  Picks the tile width from N (and requires BN == N for
