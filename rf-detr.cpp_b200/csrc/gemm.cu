@@ -310,8 +310,8 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         }
                         fence_async_smem();
                         __syncwarp();
-                        if (lane == 0 && n0 < p.N) {
-                            tma_store_3d(&tmO16, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
+                        if (lane == 0) {  // always commit: one group per staging buffer use
+                            if (n0 < p.N) tma_store_3d(&tmO16, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
                             bulk_commit();
                         }
                         ++sc;
@@ -339,11 +339,13 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                                          __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
                         fence_async_smem();
                         __syncwarp();
-                        if (lane == 0 && n0 < p.N) {
-                            if (EPI == EPI_RESID)
-                                tma_reduce_add_3d(&tmO32, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
-                            else
-                                tma_store_3d(&tmO32, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
+                        if (lane == 0) {  // always commit: one group per staging buffer use
+                            if (n0 < p.N) {
+                                if (EPI == EPI_RESID)
+                                    tma_reduce_add_3d(&tmO32, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
+                                else
+                                    tma_store_3d(&tmO32, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
+                            }
                             bulk_commit();
                         }
                         ++sc;
