@@ -2,7 +2,8 @@
 //
 //   warp 0      TMA producer (one lane): A and B K-tiles -> smem ring
 //   warp 1      TMEM allocator; one lane issues tcgen05.mma (M=128, N=BN, K=16)
-//   warps 2..5  epilogue: tcgen05.ld accumulator rows, fused epilogue, store
+//   warps 2..9  epilogue: tcgen05.ld accumulator rows, fused epilogue, TMA store
+//               (two warps per TMEM lane quadrant, each owning half the columns)
 //
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the mainloop of tile i+1.  Tiles are assigned round-robin
@@ -34,7 +35,7 @@ struct Cfg {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int OUT_STAGE = 4 * 8192;  // per epilogue warp: 2 x (32 rows x 128 B)
+    static constexpr int OUT_STAGE = 8 * 4096;  // per epilogue warp: one 32-row x 128-byte box
     static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -54,7 +55,9 @@ __device__ __forceinline__ void store_row_f32(float* dst, const float* v, int n0
 #pragma unroll
         for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     } else {
-        for (int j = 0; j < 32 && n0 + j < N; ++j) dst[j] = v[j];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (n0 + j < N) dst[j] = v[j];
     }
 }
 
@@ -75,9 +78,14 @@ __device__ __forceinline__ void store_row_f16(__half* dst, const float* v, int n
             d4[j] = u;
         }
     } else {
-        for (int j = 0; j < 32 && n0 + j < N; ++j) dst[j] = __float2half_rn(v[j]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (n0 + j < N) dst[j] = __float2half_rn(v[j]);
     }
 }
+
+// Value of lane j's register (static j after unrolling).
+__device__ __forceinline__ float bcast(float x, int j) { return __shfl_sync(0xffffffffu, x, j); }
 
 // Swizzled (128-byte pattern) staging of one 32-row x 128-byte box: thread
 // `lane` owns row `lane`; 16-byte chunk j lands at chunk (j ^ (lane & 7)).
@@ -90,8 +98,11 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+constexpr int kThreads = 320;     // 10 warps
+constexpr int kEpiThreads = 256;  // warps 2..9
+
 template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
 k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
        const __grid_constant__ CUtensorMap tmO16, const __grid_constant__ CUtensorMap tmO32, const GemmArgs p) {
     using C = Cfg<BN>;
@@ -122,7 +133,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], kEpiThreads);
         }
         *cta_abort = 0;
         fence_mbar_init();
@@ -192,10 +203,17 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         }
     } else {
         // ---------------- epilogue warps ----------------
-        const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
+        const int e = warp - 2;            // 0..7
+        const int quad = warp & 3;         // TMEM lanes [32*quad, 32*quad + 32)
+        const int half = e >> 2;           // which half of the tile's columns
         const int row_in_tile = quad * 32 + lane;
-        const uint32_t wbuf = smem_u32(out_stage + quad * 8192);
-        int sc = 0;  // staging-buffer toggle (double buffering across chunks)
+        // staging: [quad][half] boxes of 4 KB; the LN path uses both halves of its quad
+        uint8_t* wptr = out_stage + quad * 8192 + half * 4096;
+        const uint32_t wbuf = smem_u32(wptr);
+        constexpr bool kSplit = (EPI != EPI_LN) && (BN >= 128);
+        const bool active = kSplit || half == 0;
+        const int col_begin = kSplit ? half * (BN / 2) : 0;
+        const int col_end = kSplit ? col_begin + BN / 2 : BN;
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int b = tile / tiles_per_batch;
@@ -213,17 +231,20 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
             uint32_t raw[32];
             float v[32];
 
-            if constexpr (EPI == EPI_LN) {
+            if (!active) {
+                // idle warp of the LN / narrow-tile paths
+            } else if constexpr (EPI == EPI_LN) {
                 // BN == N: this thread owns the whole output row.
-                const float* rrow = p.resid ? p.resid + (size_t)m * p.ldr : nullptr;
+                const float* rrow = (p.resid && row_ok) ? p.resid + (size_t)m * p.ldr : nullptr;
                 float sum = 0.f;
                 for (int c0 = 0; c0 < BN; c0 += 32) {
                     tmem_ld32(tbase + c0, raw);
+                    const float bl = p.bias ? p.bias[c0 + lane] : 0.f;
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        float x = __uint_as_float(raw[j]) + (p.bias ? p.bias[c0 + j] : 0.f);
-                        if (rrow && row_ok) x += rrow[c0 + j];
+                        float x = __uint_as_float(raw[j]) + bcast(bl, j);
+                        if (rrow) x += rrow[c0 + j];
                         sum += x;
                     }
                 }
@@ -231,11 +252,12 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 float sq = 0.f;
                 for (int c0 = 0; c0 < BN; c0 += 32) {
                     tmem_ld32(tbase + c0, raw);
+                    const float bl = p.bias ? p.bias[c0 + lane] : 0.f;
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        float x = __uint_as_float(raw[j]) + (p.bias ? p.bias[c0 + j] : 0.f);
-                        if (rrow && row_ok) x += rrow[c0 + j];
+                        float x = __uint_as_float(raw[j]) + bcast(bl, j);
+                        if (rrow) x += rrow[c0 + j];
                         const float d = x - mean;
                         sq += d * d;
                     }
@@ -243,17 +265,19 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 const float rstd = 1.0f / sqrtf(sq / (float)BN + p.ln_eps);
                 for (int c0 = 0; c0 < BN; c0 += 32) {
                     tmem_ld32(tbase + c0, raw);
+                    const float bl = p.bias ? p.bias[c0 + lane] : 0.f;
+                    const float gl = p.ln_g[c0 + lane], bbl = p.ln_b[c0 + lane];
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        float x = __uint_as_float(raw[j]) + (p.bias ? p.bias[c0 + j] : 0.f);
-                        if (rrow && row_ok) x += rrow[c0 + j];
-                        x = (x - mean) * rstd * p.ln_g[c0 + j] + p.ln_b[c0 + j];
+                        float x = __uint_as_float(raw[j]) + bcast(bl, j);
+                        if (rrow) x += rrow[c0 + j];
+                        x = (x - mean) * rstd * bcast(gl, j) + bcast(bbl, j);
                         v[j] = act_fn(x, p.act);
                     }
                     if (p.tma_out) {
                         // f32 box [32 rows][32 cols] at wbuf, f16 box [32 rows][64 cols] at wbuf + 4096
-                        const int half = (c0 >> 5) & 1;
+                        const int hf = (c0 >> 5) & 1;
                         if (lane == 0) bulk_wait_read<0>();
                         __syncwarp();
                         if (p.out32) {
@@ -265,16 +289,16 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         if (p.out16) {
 #pragma unroll
                             for (int j = 0; j < 4; ++j)
-                                st_shared_v4(swz(wbuf + 4096, lane, j + 4 * half), pack_half2(v[8 * j], v[8 * j + 1]),
+                                st_shared_v4(swz(wbuf + 4096, lane, j + 4 * hf), pack_half2(v[8 * j], v[8 * j + 1]),
                                              pack_half2(v[8 * j + 2], v[8 * j + 3]), pack_half2(v[8 * j + 4], v[8 * j + 5]),
                                              pack_half2(v[8 * j + 6], v[8 * j + 7]));
                         }
                         fence_async_smem();
                         __syncwarp();
                         if (lane == 0) {
-                            if (p.out32) tma_store_3d(&tmO32, out_stage + quad * 8192, c0, m0w, b);
-                            if (p.out16 && (half == 1 || c0 + 32 >= BN))
-                                tma_store_3d(&tmO16, out_stage + quad * 8192 + 4096, c0 & ~63, m0w, b);
+                            if (p.out32) tma_store_3d(&tmO32, wptr, c0, m0w, b);
+                            if (p.out16 && (hf == 1 || c0 + 32 >= BN))
+                                tma_store_3d(&tmO16, wptr + 4096, c0 & ~63, m0w, b);
                             bulk_commit();
                         }
                     } else if (row_ok) {
@@ -285,94 +309,92 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
             } else if (EPI != EPI_PATCH && p.tma_out) {
                 if constexpr (EPI == EPI_F16) {
                     // 64-column chunks: one 128-byte f16 box row per thread
-                    for (int c0 = 0; c0 < BN; c0 += 64) {
+                    for (int c0 = col_begin; c0 < col_end; c0 += 64) {
                         uint32_t raw2[32];
                         tmem_ld32(tbase + c0, raw);
                         tmem_ld32(tbase + c0 + 32, raw2);
-                        tmem_wait_ld();
                         const int n0 = nt * BN + c0;
-                        const uint32_t buf = wbuf + (sc & 1) * 4096;
-                        if (lane == 0) bulk_wait_read<1>();
+                        const float b0 = (p.bias && n0 + lane < p.N) ? p.bias[n0 + lane] : 0.f;
+                        const float b1 = (p.bias && n0 + 32 + lane < p.N) ? p.bias[n0 + 32 + lane] : 0.f;
+                        tmem_wait_ld();
+                        if (lane == 0) bulk_wait_read<0>();
                         __syncwarp();
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             float w8[8];
 #pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                const int jj = 8 * j + e;
-                                const int n = n0 + jj;
-                                const float bj = (p.bias && n < p.N) ? p.bias[n] : 0.f;
-                                const uint32_t rv = jj < 32 ? raw[jj] : raw2[jj - 32];
-                                w8[e] = act_fn(__uint_as_float(rv) + bj, p.act);
+                            for (int q = 0; q < 8; ++q) {
+                                const int jj = 8 * j + q;
+                                const float rv = __uint_as_float(jj < 32 ? raw[jj] : raw2[jj - 32]);
+                                w8[q] = act_fn(rv + (jj < 32 ? bcast(b0, jj) : bcast(b1, jj - 32)), p.act);
                             }
-                            st_shared_v4(swz(buf, lane, j), pack_half2(w8[0], w8[1]), pack_half2(w8[2], w8[3]),
+                            st_shared_v4(swz(wbuf, lane, j), pack_half2(w8[0], w8[1]), pack_half2(w8[2], w8[3]),
                                          pack_half2(w8[4], w8[5]), pack_half2(w8[6], w8[7]));
                         }
                         fence_async_smem();
                         __syncwarp();
-                        if (lane == 0) {  // always commit: one group per staging buffer use
-                            if (n0 < p.N) tma_store_3d(&tmO16, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
+                        if (lane == 0) {
+                            if (n0 < p.N) tma_store_3d(&tmO16, wptr, n0, m0w, b);
                             bulk_commit();
                         }
-                        ++sc;
                     }
                 } else {
                     // f32 (store or residual reduce-add): 32-column chunks
-                    for (int c0 = 0; c0 < BN; c0 += 32) {
+                    for (int c0 = col_begin; c0 < col_end; c0 += 32) {
                         tmem_ld32(tbase + c0, raw);
-                        tmem_wait_ld();
                         const int n0 = nt * BN + c0;
+                        const bool nok = n0 + lane < p.N;
+                        const float bl = (p.bias && nok) ? p.bias[n0 + lane] : 0.f;
+                        const float sl = (EPI == EPI_RESID && p.colscale) ? (nok ? p.colscale[n0 + lane] : 0.f) : 1.f;
+                        tmem_wait_ld();
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            const int n = n0 + j;
-                            const float bj = (p.bias && n < p.N) ? p.bias[n] : 0.f;
-                            float x = act_fn(__uint_as_float(raw[j]) + bj, p.act);
-                            if (EPI == EPI_RESID && p.colscale) x *= (n < p.N ? p.colscale[n] : 0.f);
+                            float x = act_fn(__uint_as_float(raw[j]) + bcast(bl, j), p.act);
+                            if (EPI == EPI_RESID) x *= bcast(sl, j);
                             v[j] = x;
                         }
-                        const uint32_t buf = wbuf + (sc & 1) * 4096;
-                        if (lane == 0) bulk_wait_read<1>();
+                        if (lane == 0) bulk_wait_read<0>();
                         __syncwarp();
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
-                            st_shared_v4(swz(buf, lane, j), __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                            st_shared_v4(swz(wbuf, lane, j), __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
                                          __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
                         fence_async_smem();
                         __syncwarp();
-                        if (lane == 0) {  // always commit: one group per staging buffer use
+                        if (lane == 0) {
                             if (n0 < p.N) {
-                                if (EPI == EPI_RESID)
-                                    tma_reduce_add_3d(&tmO32, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
-                                else
-                                    tma_store_3d(&tmO32, out_stage + quad * 8192 + (sc & 1) * 4096, n0, m0w, b);
+                                if (EPI == EPI_RESID) tma_reduce_add_3d(&tmO32, wptr, n0, m0w, b);
+                                else tma_store_3d(&tmO32, wptr, n0, m0w, b);
                             }
                             bulk_commit();
                         }
-                        ++sc;
                     }
                 }
             } else {
-                for (int c0 = 0; c0 < BN; c0 += 32) {
+                // direct stores (PATCH remap, or outputs a TMA map cannot describe)
+                for (int c0 = col_begin; c0 < col_end; c0 += 32) {
                     tmem_ld32(tbase + c0, raw);
-                    tmem_wait_ld();
                     const int n0 = nt * BN + c0;
-                    if (!row_ok || n0 >= p.N) continue;
+                    const bool nok = n0 + lane < p.N;
+                    const float bl = (p.bias && nok) ? p.bias[n0 + lane] : 0.f;
+                    const float sl = (EPI == EPI_RESID && p.colscale && nok) ? p.colscale[n0 + lane] : 1.f;
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int n = n0 + j;
-                        const float bj = (p.bias && n < p.N) ? p.bias[n] : 0.f;
-                        v[j] = act_fn(__uint_as_float(raw[j]) + bj, p.act);
+                    for (int j = 0; j < 32; ++j) v[j] = act_fn(__uint_as_float(raw[j]) + bcast(bl, j), p.act);
+                    if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] *= bcast(sl, j);
                     }
+                    if (!row_ok || n0 >= p.N) continue;
                     if constexpr (EPI == EPI_F16) {
                         store_row_f16(p.out16 + boff + (size_t)m * p.ld16 + n0, v, n0, p.N);
                     } else if constexpr (EPI == EPI_F32) {
                         store_row_f32(p.out32 + boff + (size_t)m * p.ld32 + n0, v, n0, p.N);
                     } else if constexpr (EPI == EPI_RESID) {
                         float* dst = p.out32 + boff + (size_t)m * p.ld32 + n0;
-                        for (int j = 0; j < 32 && n0 + j < p.N; ++j) {
-                            const float s = p.colscale ? p.colscale[n0 + j] : 1.f;
-                            v[j] = dst[j] + s * v[j];
-                        }
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + j < p.N) v[j] += dst[j];
                         store_row_f32(dst, v, n0, p.N);
                     } else if constexpr (EPI == EPI_PATCH) {
                         const int img = m / p.patch_rows;
@@ -380,7 +402,9 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         const int win = rr / p.patch_tp;
                         const int tok = win * p.patch_t + 1 + (rr - win * p.patch_tp);
                         const float* pos = p.posw + (size_t)tok * p.N + n0;
-                        for (int j = 0; j < 32 && n0 + j < p.N; ++j) v[j] += pos[j];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + j < p.N) v[j] += pos[j];
                         store_row_f32(p.out32 + ((size_t)img * p.patch_ntok + tok) * p.ld32 + n0, v, n0, p.N);
                     }
                 }
@@ -472,7 +496,7 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     a.tma_out = tma ? 1 : 0;
     const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * a.batches;
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-    k_gemm<BN, EPI><<<grid, 192, Cfg<BN>::SMEM, st>>>(ta, tb, to16, to32, a);
+    k_gemm<BN, EPI><<<grid, kThreads, Cfg<BN>::SMEM, st>>>(ta, tb, to16, to32, a);
     return cudaGetLastError();
 }
 
