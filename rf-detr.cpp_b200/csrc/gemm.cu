@@ -39,13 +39,12 @@ struct Cfg {
     static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-__device__ __forceinline__ float act_fn(float v, int act) {
-    switch (act) {
-        case ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
-        case ACT_RELU: return fmaxf(v, 0.0f);
-        case ACT_SILU: return v / (1.0f + expf(-v));
-        default: return v;
-    }
+template <int ACT>
+__device__ __forceinline__ float act_fn(float v) {
+    if constexpr (ACT == ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+    else if constexpr (ACT == ACT_RELU) return fmaxf(v, 0.0f);
+    else if constexpr (ACT == ACT_SILU) return v / (1.0f + expf(-v));
+    else return v;
 }
 
 // Store 32 consecutive values of one row (columns n0..n0+31, masked by N).
@@ -101,7 +100,7 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 constexpr int kThreads = 320;     // 10 warps
 constexpr int kEpiThreads = 256;  // warps 2..9
 
-template <int BN, int EPI>
+template <int BN, int EPI, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
        const __grid_constant__ CUtensorMap tmO16, const __grid_constant__ CUtensorMap tmO32, const GemmArgs p) {
@@ -273,7 +272,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         float x = __uint_as_float(raw[j]) + bcast(bl, j);
                         if (rrow) x += rrow[c0 + j];
                         x = (x - mean) * rstd * bcast(gl, j) + bcast(bbl, j);
-                        v[j] = act_fn(x, p.act);
+                        v[j] = act_fn<ACT>(x);
                     }
                     if (p.tma_out) {
                         // f32 box [32 rows][32 cols] at wbuf, f16 box [32 rows][64 cols] at wbuf + 4096
@@ -326,7 +325,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                             for (int q = 0; q < 8; ++q) {
                                 const int jj = 8 * j + q;
                                 const float rv = __uint_as_float(jj < 32 ? raw[jj] : raw2[jj - 32]);
-                                w8[q] = act_fn(rv + (jj < 32 ? bcast(b0, jj) : bcast(b1, jj - 32)), p.act);
+                                w8[q] = act_fn<ACT>(rv + (jj < 32 ? bcast(b0, jj) : bcast(b1, jj - 32)));
                             }
                             st_shared_v4(swz(wbuf, lane, j), pack_half2(w8[0], w8[1]), pack_half2(w8[2], w8[3]),
                                          pack_half2(w8[4], w8[5]), pack_half2(w8[6], w8[7]));
@@ -349,7 +348,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         tmem_wait_ld();
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            float x = act_fn(__uint_as_float(raw[j]) + bcast(bl, j), p.act);
+                            float x = act_fn<ACT>(__uint_as_float(raw[j]) + bcast(bl, j));
                             if (EPI == EPI_RESID) x *= bcast(sl, j);
                             v[j] = x;
                         }
@@ -380,7 +379,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     const float sl = (EPI == EPI_RESID && p.colscale && nok) ? p.colscale[n0 + lane] : 1.f;
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = act_fn(__uint_as_float(raw[j]) + bcast(bl, j), p.act);
+                    for (int j = 0; j < 32; ++j) v[j] = act_fn<ACT>(__uint_as_float(raw[j]) + bcast(bl, j));
                     if constexpr (EPI == EPI_RESID) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) v[j] *= bcast(sl, j);
@@ -469,7 +468,7 @@ bool make_out_map(CUtensorMap* map, const void* base, bool f16, int cols, int ro
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int ACT>
 cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     GemmArgs a = a_in;
     static std::atomic<uint64_t> attr_set{0};  // per (BN, EPI) instantiation, one bit per device
@@ -478,7 +477,7 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_set.load() & bit)) {
-        e = cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+        e = cudaFuncSetAttribute(k_gemm<BN, EPI, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
@@ -496,16 +495,16 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     a.tma_out = tma ? 1 : 0;
     const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * a.batches;
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-    k_gemm<BN, EPI><<<grid, kThreads, Cfg<BN>::SMEM, st>>>(ta, tb, to16, to32, a);
+    k_gemm<BN, EPI, ACT><<<grid, kThreads, Cfg<BN>::SMEM, st>>>(ta, tb, to16, to32, a);
     return cudaGetLastError();
 }
 
-template <int EPI>
+template <int EPI, int ACT>
 cudaError_t dispatch_bn(const GemmArgs& a, int bn, cudaStream_t st) {
     switch (bn) {
-        case 256: return launch<256, EPI>(a, st);
-        case 128: return launch<128, EPI>(a, st);
-        default: return launch<64, EPI>(a, st);
+        case 256: return launch<256, EPI, ACT>(a, st);
+        case 128: return launch<128, EPI, ACT>(a, st);
+        default: return launch<64, EPI, ACT>(a, st);
     }
 }
 
@@ -530,12 +529,29 @@ cudaError_t gemm(const GemmArgs& a, cudaStream_t stream) {
     } else {
         bn = 64;
     }
+    // instantiated (epilogue, activation) pairs
     switch (a.epi) {
-        case EPI_F16: return dispatch_bn<EPI_F16>(a, bn, stream);
-        case EPI_F32: return dispatch_bn<EPI_F32>(a, bn, stream);
-        case EPI_RESID: return dispatch_bn<EPI_RESID>(a, bn, stream);
-        case EPI_PATCH: return dispatch_bn<EPI_PATCH>(a, bn, stream);
-        case EPI_LN: return bn == 256 ? launch<256, EPI_LN>(a, stream) : launch<128, EPI_LN>(a, stream);
+        case EPI_F16:
+            if (a.act == ACT_NONE) return dispatch_bn<EPI_F16, ACT_NONE>(a, bn, stream);
+            if (a.act == ACT_GELU) return dispatch_bn<EPI_F16, ACT_GELU>(a, bn, stream);
+            if (a.act == ACT_RELU) return dispatch_bn<EPI_F16, ACT_RELU>(a, bn, stream);
+            return cudaErrorInvalidValue;
+        case EPI_F32:
+            if (a.act == ACT_NONE) return dispatch_bn<EPI_F32, ACT_NONE>(a, bn, stream);
+            if (a.act == ACT_GELU) return dispatch_bn<EPI_F32, ACT_GELU>(a, bn, stream);
+            if (a.act == ACT_RELU) return dispatch_bn<EPI_F32, ACT_RELU>(a, bn, stream);
+            return cudaErrorInvalidValue;
+        case EPI_RESID:
+            if (a.act == ACT_NONE) return dispatch_bn<EPI_RESID, ACT_NONE>(a, bn, stream);
+            if (a.act == ACT_GELU) return dispatch_bn<EPI_RESID, ACT_GELU>(a, bn, stream);
+            return cudaErrorInvalidValue;
+        case EPI_PATCH:
+            if (a.act == ACT_NONE) return dispatch_bn<EPI_PATCH, ACT_NONE>(a, bn, stream);
+            return cudaErrorInvalidValue;
+        case EPI_LN:
+            if (a.act == ACT_NONE) return bn == 256 ? launch<256, EPI_LN, ACT_NONE>(a, stream) : launch<128, EPI_LN, ACT_NONE>(a, stream);
+            if (a.act == ACT_SILU) return bn == 256 ? launch<256, EPI_LN, ACT_SILU>(a, stream) : launch<128, EPI_LN, ACT_SILU>(a, stream);
+            return cudaErrorInvalidValue;
         default: return cudaErrorInvalidValue;
     }
 }
