@@ -123,6 +123,19 @@ int rfdetr_b200_op_attention(const void* q, const void* k, const void* v, int ld
 int rfdetr_b200_op_deform(const void* value, const float* so_aw, int ld_soaw, const float* refp, int batch, int nq,
                           int grid, int heads, int points, int dm, void* out, void* stream);
 
+/* 3x3 convolution, stride 1, zero padding 1, no bias, over channels-last f16
+ * maps (`src` rows = batch*h*w pixels, `c` channels at pitch `lds`), followed
+ * by a LayerNorm over the `oc` output channels (oc = 128 or 256) and an
+ * optional activation (0 none, 3 SiLU): the projector's ConvX block
+ * (src/projector.cpp:46-59).  weight is f16 [oc][3][3][c].  The convolution
+ * runs as an im2col into `workspace` followed by a tcgen05 GEMM with the
+ * LayerNorm fused into its epilogue; workspace must hold
+ * rfdetr_b200_op_conv3x3_workspace(batch, h, w, c) bytes of device memory. */
+size_t rfdetr_b200_op_conv3x3_workspace(int batch, int h, int w, int c);
+int rfdetr_b200_op_conv3x3(const void* src, int lds, int batch, int h, int w, int c, const void* weight, int oc,
+                           const float* ln_g, const float* ln_b, float eps, int act, float* out32, int ld32,
+                           void* out16, int ld16, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

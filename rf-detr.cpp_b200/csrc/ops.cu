@@ -40,3 +40,30 @@ extern "C" int rfdetr_b200_op_deform(const void* value, const float* so_aw, int 
     return (int)rfb::deform_sample(static_cast<const __half*>(value), so_aw, ld_soaw, refp, batch, nq, grid, heads,
                                    points, dm, static_cast<__half*>(out), static_cast<cudaStream_t>(stream));
 }
+
+extern "C" size_t rfdetr_b200_op_conv3x3_workspace(int batch, int h, int w, int c) {
+    if (batch <= 0 || h <= 0 || w <= 0 || c <= 0) return 0;
+    return (size_t)batch * h * w * 9 * c * sizeof(__half);
+}
+
+extern "C" int rfdetr_b200_op_conv3x3(const void* src, int lds, int batch, int h, int w, int c, const void* weight,
+                                      int oc, const float* ln_g, const float* ln_b, float eps, int act, float* out32,
+                                      int ld32, void* out16, int ld16, void* workspace, size_t workspace_bytes,
+                                      void* stream) {
+    const size_t need = rfdetr_b200_op_conv3x3_workspace(batch, h, w, c);
+    if (!src || !weight || !workspace || need == 0 || workspace_bytes < need) return (int)cudaErrorInvalidValue;
+    if ((oc != 128 && oc != 256) || (act != rfb::ACT_NONE && act != rfb::ACT_SILU)) return (int)cudaErrorInvalidValue;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    __half* col = static_cast<__half*>(workspace);
+    cudaError_t e = rfb::im2col3x3(static_cast<const __half*>(src), lds, batch, h, w, c, col, st);
+    if (e != cudaSuccess) return (int)e;
+    rfb::GemmArgs a;
+    a.A = col; a.lda = 9 * c;
+    a.B = static_cast<const __half*>(weight); a.ldb = 9 * c;
+    a.M = batch * h * w; a.N = oc; a.K = 9 * c;
+    a.epi = rfb::EPI_LN; a.act = act;
+    a.ln_g = ln_g; a.ln_b = ln_b; a.ln_eps = eps;
+    a.out32 = out32; a.ld32 = ld32;
+    a.out16 = static_cast<__half*>(out16); a.ld16 = ld16;
+    return (int)rfb::gemm(a, st);
+}

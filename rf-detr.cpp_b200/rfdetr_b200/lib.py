@@ -115,6 +115,10 @@ SIGNATURES = {
                                            C.c_void_p]),
     "rfdetr_b200_op_deform": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                         C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    "rfdetr_b200_op_conv3x3_workspace": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    "rfdetr_b200_op_conv3x3": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                         C.c_int, C.c_void_p, C.c_void_p, C.c_float, C.c_int, C.c_void_p, C.c_int,
+                                         C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
 }
 
 _lib = None

@@ -140,3 +140,35 @@ def test_deform_matches_grid_sample():
     s = (s * aw.permute(0, 2, 1, 3).reshape(B * H, 1, NQ, P)).sum(-1)
     ref = s.view(B, H, hd, NQ).permute(0, 3, 1, 2).reshape(B * NQ, Dm)
     assert rel(out, ref) < 2e-3
+
+
+@pytest.mark.parametrize("oc,act", [(128, 3), (256, 0)])
+def test_conv3x3_layernorm(oc, act):
+    """ConvX block (3x3 conv, channel LN, SiLU) against torch conv2d."""
+    torch.manual_seed(oc)
+    dev = "cuda:0"
+    B, H, W, Cin = 2, 9, 7, 128
+    x = torch.randn(B, H, W, Cin, device=dev).half()
+    w = (torch.randn(oc, Cin, 3, 3, device=dev) * 0.05)
+    wk = w.permute(0, 2, 3, 1).contiguous().half()  # [oc][ky][kx][c]
+    g = torch.rand(oc, device=dev) + 0.5
+    b = torch.randn(oc, device=dev) * 0.1
+    ref = F.conv2d(x.double().permute(0, 3, 1, 2), wk.double().permute(0, 3, 1, 2), padding=1)
+    ref = F.layer_norm(ref.permute(0, 2, 3, 1), (oc,), g.double(), b.double(), 1e-6)
+    if act == 3:
+        ref = F.silu(ref)
+    L = _lib()
+    ws_bytes = L.rfdetr_b200_op_conv3x3_workspace(B, H, W, Cin)
+    assert ws_bytes == B * H * W * 9 * Cin * 2
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    out16 = torch.zeros(B * H * W, oc, dtype=torch.float16, device=dev)
+    out32 = torch.zeros(B * H * W, oc, device=dev)
+    rc = L.rfdetr_b200_op_conv3x3(_p(x), Cin, B, H, W, Cin, _p(wk), oc, _p(g), _p(b), 1e-6, act, _p(out32), oc,
+                                  _p(out16), oc, _p(ws), ws_bytes, _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert rel(out32, ref.reshape(-1, oc)) < 1e-4
+    assert rel(out16, ref.reshape(-1, oc)) < 2e-3
+    # a workspace that is too small is rejected before any launch
+    assert L.rfdetr_b200_op_conv3x3(_p(x), Cin, B, H, W, Cin, _p(wk), oc, _p(g), _p(b), 1e-6, act, _p(out32), oc,
+                                    _p(out16), oc, _p(ws), ws_bytes - 1, _stream()) != 0
