@@ -136,6 +136,23 @@ int rfdetr_b200_op_conv3x3(const void* src, int lds, int batch, int h, int w, in
                            const float* ln_g, const float* ln_b, float eps, int act, float* out32, int ld32,
                            void* out16, int ld16, void* workspace, size_t workspace_bytes, void* stream);
 
+/* rfdetr_b200_op_conv3x3 without the workspace argument, for callers that
+ * cannot call cudaMalloc (a latency-critical serving loop that cannot absorb
+ * cudaMalloc's device-wide synchronization, a host whose memory is owned by
+ * another framework's caching allocator, a plugin that only receives device
+ * pointers).  No counterpart in the reference.  It allocates nothing: the
+ * im2col scratch is a fixed array of 8 Mi f16 values (16 MiB) in the library's
+ * device memory, present on every GPU that loads the library until exit, so
+ * batch*h*w*9*c must not exceed 8388608 (larger sizes are rejected with an
+ * error message and cudaErrorInvalidValue).  The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) — make that first call
+ * before any stream capture.  All calls on a device share the array: calls
+ * whose work overlaps on the GPU race; calls in one stream are safe.  The
+ * caller still passes inputs and outputs; arguments as rfdetr_b200_op_conv3x3. */
+int rfdetr_b200_op_conv3x3_noalloc(const void* src, int lds, int batch, int h, int w, int c, const void* weight,
+                                   int oc, const float* ln_g, const float* ln_b, float eps, int act, float* out32,
+                                   int ld32, void* out16, int ld16, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -119,6 +119,9 @@ SIGNATURES = {
     "rfdetr_b200_op_conv3x3": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                          C.c_int, C.c_void_p, C.c_void_p, C.c_float, C.c_int, C.c_void_p, C.c_int,
                                          C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "rfdetr_b200_op_conv3x3_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                 C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_float, C.c_int,
+                                                 C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]),
 }
 
 _lib = None
