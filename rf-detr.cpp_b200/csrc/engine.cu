@@ -523,12 +523,15 @@ rfdetr_status Engine::enqueue(int B, const uint8_t* src_rgb, int src_w, int src_
     const int Mb = B * Ntok_, Mp = B * G * G, Mq = B * NQ;
 
     // ---- input
+    // ---- preprocess + patch im2col in windowed order (one kernel from uint8)
     if (src_rgb) {
         if (src_w <= 0 || src_h <= 0) return RFDETR_ERR_INVALID_ARG;
-        L.check(preprocess_u8(src_rgb, B, src_w, src_h, S_, cfg_.mean, cfg_.std, img_, st), "preprocess");
+        L.check(patch_from_rgb(src_rgb, B, src_w, src_h, S_, P_, nw_, Kpad_, cfg_.mean, cfg_.std, apatch_, st),
+                "patch_from_rgb");
+    } else {
+        L.check(patch_im2col(img_, B, S_, P_, nw_, Kpad_, apatch_, st), "patch_im2col");
     }
     // ---- patch embed into windowed tokens (+ pos), CLS rows
-    L.check(patch_im2col(img_, B, S_, P_, nw_, Kpad_, apatch_, st), "patch_im2col");
     {
         GemmArgs a;
         a.A = apatch_; a.lda = Kpad_; a.B = patch_.w; a.ldb = patch_.ldw;

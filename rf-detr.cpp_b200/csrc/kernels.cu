@@ -80,6 +80,47 @@ __global__ void k_patch_im2col(const float* __restrict__ img, int B, int S, int 
     A[i] = __float2half_rn(v);
 }
 
+// Preprocess (src/image_io.cpp:207-248) fused into the patch im2col: each
+// im2col element is one normalized model-resolution pixel, sampled straight
+// from the uint8 source with the same double-precision source coordinates.
+__global__ void k_patch_from_rgb(const uint8_t* __restrict__ rgb, int B, int w, int h, int S, int p, int nw, int Kpad,
+                                 float m0, float m1, float m2, float s0, float s1, float s2, __half* __restrict__ A) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int G = S / p, ws = G / nw, Tp = ws * ws;
+    const size_t rows = (size_t)B * nw * nw * Tp;
+    if (i >= rows * Kpad) return;
+    const size_t row = i / Kpad;
+    const int k = (int)(i - row * Kpad);
+    float v = 0.f;
+    if (k < 3 * p * p) {
+        const int b = (int)(row / ((size_t)nw * nw * Tp));
+        const int rr = (int)(row - (size_t)b * nw * nw * Tp);
+        const int win = rr / Tp, t = rr - win * Tp;
+        const int gy = (win / nw) * ws + t / ws, gx = (win % nw) * ws + t % ws;
+        const int c = k / (p * p), ky = (k / p) % p, kx = k % p;
+        const int yy = gy * p + ky, xx = gx * p + kx;
+        const double scx = (double)w / (double)S, scy = (double)h / (double)S;
+        const double fy = ((double)yy + 0.5) * scy - 0.5;
+        const int y0r = (int)floor(fy);
+        const int y0 = min(max(y0r, 0), h - 1), y1 = min(max(y0r + 1, 0), h - 1);
+        const float wy = (float)(fy - (double)y0r);
+        const double fx = ((double)xx + 0.5) * scx - 0.5;
+        const int x0r = (int)floor(fx);
+        const int x0 = min(max(x0r, 0), w - 1), x1 = min(max(x0r + 1, 0), w - 1);
+        const float wx = (float)(fx - (double)x0r);
+        const uint8_t* img = rgb + (size_t)b * h * w * 3;
+        const float p00 = (float)img[((size_t)y0 * w + x0) * 3 + c];
+        const float p01 = (float)img[((size_t)y0 * w + x1) * 3 + c];
+        const float p10 = (float)img[((size_t)y1 * w + x0) * 3 + c];
+        const float p11 = (float)img[((size_t)y1 * w + x1) * 3 + c];
+        const float top = p00 + (p01 - p00) * wx;
+        const float bot = p10 + (p11 - p10) * wx;
+        const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2), sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+        v = ((top + (bot - top) * wy) / 255.0f - mean) / sd;
+    }
+    A[i] = __float2half_rn(v);
+}
+
 __global__ void k_cls_rows(float* __restrict__ x, const float* __restrict__ clsrow, int B, int NW, int T, int D) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)B * NW * D) return;
@@ -120,6 +161,51 @@ __global__ void k_layernorm(const float* x, int rows, int D, const float* __rest
             const float o = (v[i] - mean) * rstd * g[c] + b[c];
             if (y32) y32[(size_t)row * D + c] = o;
             if (y16) y16[(size_t)row * D + c] = __float2half_rn(o);
+        }
+    }
+}
+
+// Same, 16-byte vectors: lane owns columns 4*(lane + 32*i) .. +3, D = 128*NV.
+template <int NV>
+__global__ void k_layernorm_v4(const float* x, int rows, const float* __restrict__ g, const float* __restrict__ b,
+                               float eps, float* y32, __half* __restrict__ y16) {
+    constexpr int D = 128 * NV;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * D);
+    float4 v[NV];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        v[i] = xr[lane + 32 * i];
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+    const float mean = warp_sum(s) / (float)D;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const float a = v[i].x - mean, bq = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+        q += (a * a + bq * bq) + (c * c + d * d);
+    }
+    const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c0 = 4 * (lane + 32 * i);
+        const float4 gg = *reinterpret_cast<const float4*>(g + c0);
+        const float4 bb = *reinterpret_cast<const float4*>(b + c0);
+        float4 o;
+        o.x = (v[i].x - mean) * rstd * gg.x + bb.x;
+        o.y = (v[i].y - mean) * rstd * gg.y + bb.y;
+        o.z = (v[i].z - mean) * rstd * gg.z + bb.z;
+        o.w = (v[i].w - mean) * rstd * gg.w + bb.w;
+        if (y32) *reinterpret_cast<float4*>(y32 + (size_t)row * D + c0) = o;
+        if (y16) {
+            __half2 h0 = __floats2half2_rn(o.x, o.y), h1 = __floats2half2_rn(o.z, o.w);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t*>(&h0);
+            u.y = *reinterpret_cast<uint32_t*>(&h1);
+            *reinterpret_cast<uint2*>(y16 + (size_t)row * D + c0) = u;
         }
     }
 }
@@ -473,6 +559,15 @@ cudaError_t patch_im2col(const float* img, int B, int S, int p, int nw, int Kpad
     return cudaGetLastError();
 }
 
+cudaError_t patch_from_rgb(const uint8_t* rgb, int B, int w, int h, int S, int p, int nw, int Kpad,
+                           const float* mean3, const float* std3, __half* A, cudaStream_t st) {
+    const int G = S / p, Tp = (G / nw) * (G / nw);
+    const size_t n = (size_t)B * nw * nw * Tp * Kpad;
+    k_patch_from_rgb<<<cdiv(n, 256), 256, 0, st>>>(rgb, B, w, h, S, p, nw, Kpad, mean3[0], mean3[1], mean3[2],
+                                                   std3[0], std3[1], std3[2], A);
+    return cudaGetLastError();
+}
+
 cudaError_t write_cls_rows(float* x, const float* clsrow, int B, int NW, int T, int D, cudaStream_t st) {
     const size_t n = (size_t)B * NW * D;
     k_cls_rows<<<cdiv(n, 256), 256, 0, st>>>(x, clsrow, B, NW, T, D);
@@ -483,7 +578,10 @@ cudaError_t layernorm(const float* x, int rows, int D, const float* g, const flo
                       __half* y16, cudaStream_t st) {
     if (D > 512) return cudaErrorInvalidValue;
     const unsigned blocks = cdiv(rows, 8);
-    if (D <= 256) k_layernorm<8><<<blocks, 256, 0, st>>>(x, rows, D, g, b, eps, y32, y16);
+    const bool vec = (D % 128 == 0) && !(((uintptr_t)x | (uintptr_t)y32 | (uintptr_t)y16) & 15);
+    if (vec && D == 384) k_layernorm_v4<3><<<blocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16);
+    else if (vec && D == 256) k_layernorm_v4<2><<<blocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16);
+    else if (D <= 256) k_layernorm<8><<<blocks, 256, 0, st>>>(x, rows, D, g, b, eps, y32, y16);
     else k_layernorm<16><<<blocks, 256, 0, st>>>(x, rows, D, g, b, eps, y32, y16);
     return cudaGetLastError();
 }

@@ -23,6 +23,10 @@ cudaError_t preprocess_u8(const uint8_t* rgb, int B, int w, int h, int S, const 
 // K ordered (channel, ky, kx), zero padded to Kpad.
 cudaError_t patch_im2col(const float* img, int B, int S, int p, int nw, int Kpad, __half* A, cudaStream_t st);
 
+// Preprocess fused with the patch im2col: uint8 HWC [B][h][w][3] -> A as above.
+cudaError_t patch_from_rgb(const uint8_t* rgb, int B, int w, int h, int S, int p, int nw, int Kpad,
+                           const float* mean3, const float* std3, __half* A, cudaStream_t st);
+
 // x[b][w*T] = clsrow (one CLS token per window).
 cudaError_t write_cls_rows(float* x, const float* clsrow, int B, int NW, int T, int D, cudaStream_t st);
 

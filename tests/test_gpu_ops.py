@@ -37,7 +37,7 @@ GEMM_SHAPES = [(300, 256, 256), (1000, 1152, 384), (517, 91, 256), (200, 4, 256)
 
 
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
-@pytest.mark.parametrize("epi,act", [(0, 0), (1, 0), (0, 1), (0, 2), (2, 0)])
+@pytest.mark.parametrize("epi,act", [(0, 0), (1, 0), (0, 1), (0, 2), (2, 0), (1, 1)])
 def test_gemm(M, N, K, epi, act):
     torch.manual_seed(M * 7 + N + K)
     dev = "cuda:0"
@@ -172,3 +172,4 @@ def test_conv3x3_layernorm(oc, act):
     # a workspace that is too small is rejected before any launch
     assert L.rfdetr_b200_op_conv3x3(_p(x), Cin, B, H, W, Cin, _p(wk), oc, _p(g), _p(b), 1e-6, act, _p(out32), oc,
                                     _p(out16), oc, _p(ws), ws_bytes - 1, _stream()) != 0
+
