@@ -39,18 +39,31 @@ struct Cfg {
     static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-// erf-GELU, 0.5 v (1 + erf(v / sqrt 2)), with erf from Abramowitz & Stegun,
-// Handbook of Mathematical Functions, eq. 7.1.26 (Hastings' rational
-// approximation): erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^{-z^2},
-// t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7.  About half the instructions of a
-// library erff, which matters because this runs once per fc1 / MLP output.
+// erf-GELU, 0.5 v (1 + erf(v / sqrt 2)).
+#ifndef RFB_GELU_AS
+#define RFB_GELU_AS 1
+#endif
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
 __device__ __forceinline__ float gelu_erf(float v) {
+#if RFB_GELU_AS
+    // erf from Abramowitz & Stegun, Handbook of Mathematical Functions,
+    // eq. 7.1.26 (Hastings' rational approximation):
+    // erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^{-z^2},
+    // t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7.
     const float z = fabsf(v) * 0.70710678118654752440f;
-    const float t = __frcp_rn(fmaf(0.3275911f, z, 1.0f));
+    const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
     const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f),
                                         -0.284496736f), 0.254829592f);
     const float erf_abs = fmaf(-poly, __expf(-z * z), 1.0f);
-    return 0.5f * v * (1.0f + copysignf(erf_abs, v));
+    const float erf_v = __int_as_float(__float_as_int(erf_abs) | (__float_as_int(v) & 0x80000000));
+    return 0.5f * v * (1.0f + erf_v);
+#else
+    return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+#endif
 }
 
 template <int ACT>

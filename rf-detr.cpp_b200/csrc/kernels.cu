@@ -99,6 +99,13 @@ __global__ void k_patch_from_rgb(const uint8_t* __restrict__ rgb, int B, int w, 
         const int gy = (win / nw) * ws + t / ws, gx = (win % nw) * ws + t % ws;
         const int c = k / (p * p), ky = (k / p) % p, kx = k % p;
         const int yy = gy * p + ky, xx = gx * p + kx;
+        const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2), sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+        if (w == S && h == S) {
+            // identity resize: source coordinate == destination, interpolation weights 0
+            const float px = (float)rgb[(((size_t)b * h + yy) * w + xx) * 3 + c];
+            A[i] = __float2half_rn((px / 255.0f - mean) / sd);
+            return;
+        }
         const double scx = (double)w / (double)S, scy = (double)h / (double)S;
         const double fy = ((double)yy + 0.5) * scy - 0.5;
         const int y0r = (int)floor(fy);
@@ -115,7 +122,6 @@ __global__ void k_patch_from_rgb(const uint8_t* __restrict__ rgb, int B, int w, 
         const float p11 = (float)img[((size_t)y1 * w + x1) * 3 + c];
         const float top = p00 + (p01 - p00) * wx;
         const float bot = p10 + (p11 - p10) * wx;
-        const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2), sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
         v = ((top + (bot - top) * wy) / 255.0f - mean) / sd;
     }
     A[i] = __float2half_rn(v);

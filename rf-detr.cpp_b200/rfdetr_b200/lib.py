@@ -13,7 +13,7 @@ import os
 import numpy as np
 
 PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(PKG, "lib", "librfdetr.so")
+LIB_PATH = os.environ.get("RFDETR_LIB", os.path.join(PKG, "lib", "librfdetr.so"))
 
 RFDETR_OK = 0
 STATUS = {0: "ok", -1: "invalid argument", -2: "file not found", -3: "i/o error", -4: "out of memory",
