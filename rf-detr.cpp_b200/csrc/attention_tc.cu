@@ -1,0 +1,323 @@
+// Fused multi-head attention on the 5th-generation tensor cores (head_dim 64):
+// the windowed and global blocks of the DINOv2 backbone.
+//
+// One CTA = 128 query rows of one (group, head); keys in blocks of 64.
+//   warp 0      TMA: Q once, then K/V blocks into a 2-slot ring (3-D tensor
+//               maps (column, token, group): rows past the sequence end load
+//               as zeros)
+//   warp 1      TMEM allocation; one lane issues tcgen05.mma:
+//                 S = Q K^T            (M=128, N=64,  K=64)  -> TMEM cols [0, 64)
+//                 O += P V             (M=128, N=64,  K=64)  -> TMEM cols [64, 128)
+//               S of block j+1 is issued as soon as the softmax has read S_j.
+//   warps 2..5  one thread per query row: read S_j from TMEM, online softmax in
+//               f32 (exp2 domain), rescale O in TMEM when the row max moves,
+//               write P_j (f16) into 128B-swizzled shared memory as the A
+//               operand of the P V product; at the end O / l -> f16 -> TMA store
+//               (3-D map clips rows past the sequence end).
+// V is consumed in its natural [key][dim] layout as an MN-major B operand.
+// Every mbarrier wait is bounded (see sm100.cuh).
+#include "kernels.cuh"
+#include "sm100.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
+
+namespace rfb {
+
+namespace {
+
+constexpr int AQ = 128;                 // query rows per CTA
+constexpr int AK = 64;                  // keys per block
+constexpr int HD = 64;                  // head dim
+constexpr int Q_BYTES = AQ * HD * 2;    // 16 KB
+constexpr int KV_BYTES = AK * HD * 2;   // 8 KB
+constexpr int P_BYTES = AQ * AK * 2;    // 16 KB
+constexpr int SMEM_TILES = Q_BYTES + 4 * KV_BYTES + P_BYTES;  // 64 KB
+constexpr int SMEM = SMEM_TILES + 1024 + 256;
+constexpr int TMEM_COLS = 128;          // S: [0,64), O: [64,128)
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t swz(uint32_t base, int row, int j) {
+    return base + row * 128 + ((j ^ (row & 7)) << 4);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(192, 2)
+k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, int L, float sl2,
+          int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + Q_BYTES;            // 2 slots
+    uint8_t* sV = sK + 2 * KV_BYTES;       // 2 slots
+    uint8_t* sP = sV + 2 * KV_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_TILES);
+    uint64_t* q_full = bars + 0;
+    uint64_t* kv_full = bars + 1;   // [2]
+    uint64_t* kv_empty = bars + 3;  // [2]
+    uint64_t* s_full = bars + 5;
+    uint64_t* s_free = bars + 6;
+    uint64_t* p_full = bars + 7;
+    uint64_t* pv_done = bars + 8;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 9);
+    volatile int* cta_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * AQ;
+    const int head = blockIdx.y;
+    const int g = blockIdx.z;
+    const int nb = (L + AK - 1) / AK;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        mbar_init(&kv_full[0], 1);
+        mbar_init(&kv_full[1], 1);
+        mbar_init(&kv_empty[0], 1);
+        mbar_init(&kv_empty[1], 1);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 128);
+        mbar_init(p_full, 128);
+        mbar_init(pv_done, 1);
+        *cta_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    const uint32_t tS = tmem, tO = tmem + AK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            mbar_arrive_expect_tx(q_full, Q_BYTES);
+            tma_load_3d(&tmQ, q_full, sQ, head * HD, q0, g);
+            for (int j = 0; j < nb; ++j) {
+                const int slot = j & 1;
+                if (!mbar_wait(&kv_empty[slot], ((j >> 1) & 1) ^ 1, cta_abort, err)) break;
+                mbar_arrive_expect_tx(&kv_full[slot], 2 * KV_BYTES);
+                tma_load_3d(&tmK, &kv_full[slot], sK + slot * KV_BYTES, head * HD, j * AK, g);
+                tma_load_3d(&tmV, &kv_full[slot], sV + slot * KV_BYTES, head * HD, j * AK, g);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t IDESC_S = idesc_f16_f32(AQ, AK);
+            constexpr uint32_t IDESC_PV = idesc_f16_f32(AQ, HD) | (1u << 16);  // B (V) MN-major
+            const uint32_t q_s = smem_u32(sQ), p_s = smem_u32(sP);
+            bool ok = mbar_wait(q_full, 0, cta_abort, err) && mbar_wait(&kv_full[0], 0, cta_abort, err);
+            if (ok) {
+                tc_fence_after();
+                const uint32_t k_s = smem_u32(sK);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    umma_f16(tS, sw128_kmajor_desc(q_s + kk * 32), sw128_kmajor_desc(k_s + kk * 32), IDESC_S, kk > 0);
+                umma_commit(s_full);
+            }
+            for (int j = 0; ok && j < nb; ++j) {
+                const int slot = j & 1;
+                if (j + 1 < nb) {
+                    const int ns = (j + 1) & 1;
+                    if (!mbar_wait(s_free, j & 1, cta_abort, err)) break;
+                    if (!mbar_wait(&kv_full[ns], ((j + 1) >> 1) & 1, cta_abort, err)) break;
+                    tc_fence_after();
+                    const uint32_t k_s = smem_u32(sK + ns * KV_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk)
+                        umma_f16(tS, sw128_kmajor_desc(q_s + kk * 32), sw128_kmajor_desc(k_s + kk * 32), IDESC_S,
+                                 kk > 0);
+                    umma_commit(s_full);
+                }
+                if (!mbar_wait(p_full, j & 1, cta_abort, err)) break;
+                tc_fence_after();
+                const uint32_t v_s = smem_u32(sV + slot * KV_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < AK / 16; ++kk)
+                    umma_f16(tO, sw128_kmajor_desc(p_s + kk * 32), sw128_kmajor_desc(v_s + kk * 2048), IDESC_PV,
+                             (j > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(pv_done);
+                umma_commit(&kv_empty[slot]);
+            }
+        }
+    } else {
+        // ---- softmax warps: thread = query row (q0 + quad*32 + lane)
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const uint32_t lanebase = (uint32_t)(quad * 32) << 16;
+        const uint32_t p_s = smem_u32(sP);
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nb; ++j) {
+            if (!mbar_wait(s_full, j & 1, cta_abort, err)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t r0[32], r1[32];
+            tmem_ld32(tS + lanebase, r0);
+            tmem_ld32(tS + lanebase + 32, r1);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(s_free);
+            const int kbase = j * AK;
+            const bool full_block = kbase + AK <= L;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                float x0 = __uint_as_float(r0[e]) * sl2, x1 = __uint_as_float(r1[e]) * sl2;
+                if (!full_block) {
+                    if (kbase + e >= L) x0 = -INFINITY;
+                    if (kbase + 32 + e >= L) x1 = -INFINITY;
+                }
+                r0[e] = __float_as_uint(x0);
+                r1[e] = __float_as_uint(x1);
+                mx = fmaxf(mx, fmaxf(x0, x1));
+            }
+            const float m_new = fmaxf(m, mx);
+            const float alpha = ex2(m - m_new);  // 0 on the first block (m = -inf)
+            float rs = 0.f;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const float p0 = ex2(__uint_as_float(r0[e]) - m_new);
+                const float p1 = ex2(__uint_as_float(r1[e]) - m_new);
+                r0[e] = __float_as_uint(p0);
+                r1[e] = __float_as_uint(p1);
+                rs += p0 + p1;
+            }
+            l = l * alpha + rs;
+            m = m_new;
+            if (j > 0) {
+                // previous P V done: P buffer reusable, O stable for the rescale
+                if (!mbar_wait(pv_done, (j - 1) & 1, cta_abort, err)) { ok = false; break; }
+                tc_fence_after();
+            }
+            // P (f16) row -> swizzled K-major tile [128 rows][64 keys]: 16-byte chunk cc holds keys 8cc..8cc+7
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                const int o = (cc & 3) * 8;
+                float w[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) w[e] = __uint_as_float(cc < 4 ? r0[o + e] : r1[o + e]);
+                st_shared_v4(swz(p_s, row, cc), pack_half2(w[0], w[1]), pack_half2(w[2], w[3]), pack_half2(w[4], w[5]),
+                             pack_half2(w[6], w[7]));
+            }
+            if (j > 0) {
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                    uint32_t o[32];
+#pragma unroll
+                    for (int c = 0; c < HD; c += 32) {
+                        tmem_ld32(tO + lanebase + c, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st32(tO + lanebase + c, o);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && mbar_wait(pv_done, (nb - 1) & 1, cta_abort, err)) {
+            tc_fence_after();
+            const float inv = 1.0f / l;
+            // stage O / l as f16 in this warp's quarter of the (now idle) P buffer
+            uint8_t* stage = sP + quad * 4096;
+            const uint32_t st_s = smem_u32(stage);
+            uint32_t o[32];
+#pragma unroll
+            for (int c = 0; c < HD; c += 32) {
+                tmem_ld32(tO + lanebase + c, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    st_shared_v4(swz(st_s, lane, (c >> 3) + q),
+                                 pack_half2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                 pack_half2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                 pack_half2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                 pack_half2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_3d(&tmO, stage, head * HD, q0 + quad * 32, g);
+                bulk_commit();
+                bulk_wait<0>();
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
+std::once_flag g_enc_once;
+
+bool encode_fn() {
+    std::call_once(g_enc_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_enc != nullptr;
+}
+
+// (cols, seq, group) view of a [groups*seq][ld] f16 matrix; box of `rows` x 64 columns.
+bool make_seq_map(CUtensorMap* m, const void* base, int cols, int seq, int groups, int ld, int rows) {
+    if (((uintptr_t)base & 15) || (ld % 8)) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)seq, (cuuint64_t)groups};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)seq * ld * 2};
+    cuuint32_t box[3] = {(cuuint32_t)HD, (cuuint32_t)rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return g_enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t attention_tc(const __half* q, const __half* k, const __half* v, int ldq, int ldk, int ldv, __half* o,
+                         int ldo, int seq_len, int groups, int heads, float scale, int* err, cudaStream_t st) {
+    if (seq_len <= 0 || groups <= 0) return cudaSuccess;
+    if (!encode_fn()) return cudaErrorNotSupported;
+    static std::atomic<uint64_t> attr_set{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+        e = cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        if (e != cudaSuccess) return e;
+        attr_set.fetch_or(bit);
+    }
+    const int cols = heads * HD;
+    CUtensorMap mq, mk, mv, mo;
+    if (!make_seq_map(&mq, q, cols, seq_len, groups, ldq, AQ) || !make_seq_map(&mk, k, cols, seq_len, groups, ldk, AK) ||
+        !make_seq_map(&mv, v, cols, seq_len, groups, ldv, AK) || !make_seq_map(&mo, o, cols, seq_len, groups, ldo, 32))
+        return cudaErrorInvalidValue;
+    const dim3 grid((seq_len + AQ - 1) / AQ, heads, groups);
+    k_attn_tc<<<grid, 192, SMEM, st>>>(mq, mk, mv, mo, seq_len, scale * 1.4426950408889634f, err);
+    return cudaGetLastError();
+}
+
+}  // namespace rfb

@@ -550,11 +550,12 @@ rfdetr_status Engine::enqueue(int B, const uint8_t* src_rgb, int src_w, int src_
         L.check(layernorm(x_, Mb, D, bk.ln1.g, bk.ln1.b, 1e-6f, nullptr, h16_, st), "ln1");
         L.gemm("qkv", h16_, D, Mb, bk.qkv, EPI_F16, ACT_NONE, nullptr, 0, qkv_, 3 * D);
         if (bk.global)
-            L.check(attention(qkv_, qkv_ + D, qkv_ + 2 * D, 3 * D, 3 * D, 3 * D, attn_, D, Ntok_, B, H_, D / H_, scale, st),
+            L.check(attention_tc(qkv_, qkv_ + D, qkv_ + 2 * D, 3 * D, 3 * D, 3 * D, attn_, D, Ntok_, B, H_, scale, d_err_,
+                                 st),
                     "attn_global");
         else
-            L.check(attention(qkv_, qkv_ + D, qkv_ + 2 * D, 3 * D, 3 * D, 3 * D, attn_, D, T_, B * NW_, H_, D / H_, scale,
-                              st),
+            L.check(attention_tc(qkv_, qkv_ + D, qkv_ + 2 * D, 3 * D, 3 * D, 3 * D, attn_, D, T_, B * NW_, H_, scale,
+                                 d_err_, st),
                     "attn_window");
         L.gemm("proj", attn_, D, Mb, bk.proj, EPI_RESID, ACT_NONE, x_, D, nullptr, 0, bk.ls1);
         L.check(layernorm(x_, Mb, D, bk.ln2.g, bk.ln2.b, 1e-6f, nullptr, h16_, st), "ln2");

@@ -14,6 +14,12 @@ namespace rfb {
 cudaError_t attention(const __half* q, const __half* k, const __half* v, int ldq, int ldk, int ldv, __half* o,
                       int ldo, int seq_len, int groups, int heads, int head_dim, float scale, cudaStream_t st);
 
+// Same computation on the tcgen05 tensor cores (head_dim 64 only): S and O in
+// TMEM, P staged in shared memory.  `err` (may be null) receives the device
+// error word on a bounded-wait timeout.
+cudaError_t attention_tc(const __half* q, const __half* k, const __half* v, int ldq, int ldk, int ldv, __half* o,
+                         int ldo, int seq_len, int groups, int heads, float scale, int* err, cudaStream_t st);
+
 // uint8 HWC images [B][h][w][3] -> planar normalized f32 [B][3][S][S]
 // (bilinear, half-pixel centres, double-precision source coordinates).
 cudaError_t preprocess_u8(const uint8_t* rgb, int B, int w, int h, int S, const float* mean3, const float* std3,

@@ -30,6 +30,10 @@ extern "C" int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ld
 extern "C" int rfdetr_b200_op_attention(const void* q, const void* k, const void* v, int ldq, int ldk, int ldv,
                                         void* o, int ldo, int seq_len, int groups, int heads, int head_dim,
                                         float scale, void* stream) {
+    if (head_dim == 64)
+        return (int)rfb::attention_tc(static_cast<const __half*>(q), static_cast<const __half*>(k),
+                                      static_cast<const __half*>(v), ldq, ldk, ldv, static_cast<__half*>(o), ldo,
+                                      seq_len, groups, heads, scale, nullptr, static_cast<cudaStream_t>(stream));
     return (int)rfb::attention(static_cast<const __half*>(q), static_cast<const __half*>(k),
                                static_cast<const __half*>(v), ldq, ldk, ldv, static_cast<__half*>(o), ldo, seq_len,
                                groups, heads, head_dim, scale, static_cast<cudaStream_t>(stream));
