@@ -175,25 +175,25 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             mbar_arrive(s_free);
             const int kbase = j * AK;
             const bool full_block = kbase + AK <= L;
-            float mx = -INFINITY;
+            float mx = -INFINITY;  // row max of raw scores (scale > 0 commutes with max)
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-                float x0 = __uint_as_float(r0[e]) * sl2, x1 = __uint_as_float(r1[e]) * sl2;
+                float x0 = __uint_as_float(r0[e]), x1 = __uint_as_float(r1[e]);
                 if (!full_block) {
                     if (kbase + e >= L) x0 = -INFINITY;
                     if (kbase + 32 + e >= L) x1 = -INFINITY;
+                    r0[e] = __float_as_uint(x0);
+                    r1[e] = __float_as_uint(x1);
                 }
-                r0[e] = __float_as_uint(x0);
-                r1[e] = __float_as_uint(x1);
                 mx = fmaxf(mx, fmaxf(x0, x1));
             }
-            const float m_new = fmaxf(m, mx);
-            const float alpha = ex2(m - m_new);  // 0 on the first block (m = -inf)
+            const float m_new = fmaxf(m, mx * sl2);  // running max in log2 units
+            const float alpha = ex2(m - m_new);      // 0 on the first block (m = -inf)
             float rs = 0.f;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-                const float p0 = ex2(__uint_as_float(r0[e]) - m_new);
-                const float p1 = ex2(__uint_as_float(r1[e]) - m_new);
+                const float p0 = ex2(fmaf(__uint_as_float(r0[e]), sl2, -m_new));
+                const float p1 = ex2(fmaf(__uint_as_float(r1[e]), sl2, -m_new));
                 r0[e] = __float_as_uint(p0);
                 r1[e] = __float_as_uint(p1);
                 rs += p0 + p1;

@@ -27,6 +27,7 @@ uint16_t f2h_bits(float f) {
 
 Engine::~Engine() {
     if (device_ >= 0) cudaSetDevice(device_);
+    drop_graphs();
     free_activations();
     if (rgb_u8_) cudaFree(rgb_u8_);
     for (void* p : wallocs_) cudaFree(p);
@@ -64,6 +65,7 @@ std::unique_ptr<Engine> Engine::create(const Model& m, int device, int max_batch
     std::unique_ptr<Engine> e(new Engine());
     e->cfg_ = m.cfg;
     e->device_ = device;
+    if (const char* ng = std::getenv("RFDETR_NO_GRAPH")) e->use_graphs_ = ng[0] == '0';
     if (RFB_CUDA_FAIL(cudaStreamCreateWithFlags(&e->stream_, cudaStreamNonBlocking))) {
         set(RFDETR_ERR_INFERENCE);
         return nullptr;
@@ -377,6 +379,7 @@ rfdetr_status Engine::reserve_rgb(size_t bytes) {
 }
 
 rfdetr_status Engine::alloc_activations(int B) {
+    drop_graphs();  // captured graphs hold the old buffer addresses
     free_activations();
     const size_t Mb = (size_t)B * Ntok_;       // backbone rows
     const size_t Mp = (size_t)B * G_ * G_;      // spatial rows
@@ -507,7 +510,54 @@ struct Launcher {
 
 }  // namespace
 
+void Engine::drop_graphs() {
+    for (auto& g : graphs_) cudaGraphExecDestroy(g.exec);
+    graphs_.clear();
+}
+
 rfdetr_status Engine::enqueue(int B, const uint8_t* src_rgb, int src_w, int src_h) {
+    if (!use_graphs_ || profiling_) return enqueue_raw(B, src_rgb, src_w, src_h);
+    if (RFB_CUDA_FAIL(cudaSetDevice(device_))) return RFDETR_ERR_INFERENCE;
+    for (auto& g : graphs_) {
+        if (g.batch == B && g.src == src_rgb && g.w == src_w && g.h == src_h) {
+            return RFB_CUDA_FAIL(cudaGraphLaunch(g.exec, stream_)) ? RFDETR_ERR_INFERENCE : RFDETR_OK;
+        }
+    }
+    // First time for this shape / input: run it directly (this also performs
+    // any one-time per-device kernel set-up), then capture the same sequence
+    // for the next calls.
+    rfdetr_status s = enqueue_raw(B, src_rgb, src_w, src_h);
+    if (s != RFDETR_OK) return s;
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return RFDETR_OK;  // capture unavailable: keep launching directly
+    }
+    const int launches = launches_;
+    const rfdetr_status cs = enqueue_raw(B, src_rgb, src_w, src_h);
+    const cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
+    launches_ = launches;
+    if (cs != RFDETR_OK || ce != cudaSuccess || !graph) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        return RFDETR_OK;
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) {
+        cudaGetLastError();
+        return RFDETR_OK;
+    }
+    if (graphs_.size() >= 16) {
+        cudaGraphExecDestroy(graphs_.front().exec);
+        graphs_.erase(graphs_.begin());
+    }
+    graphs_.push_back({B, src_rgb, src_w, src_h, exec});
+    return RFDETR_OK;
+}
+
+rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int src_h) {
     if (B <= 0 || B > max_batch_) return RFDETR_ERR_INVALID_ARG;
     if (RFB_CUDA_FAIL(cudaSetDevice(device_))) return RFDETR_ERR_INFERENCE;
     Launcher L{stream_, d_err_};

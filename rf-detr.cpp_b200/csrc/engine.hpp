@@ -53,6 +53,10 @@ public:
     // (device pointer, batch x src_h x src_w x 3 uint8) it is preprocessed
     // first; otherwise d_planar() holds the already-normalized input.
     // Asynchronous; call finish() to synchronize.
+    // The launch sequence is captured into a CUDA graph the first time a
+    // (batch, input pointer, input size) combination is seen and replayed
+    // afterwards (RFDETR_NO_GRAPH=1 disables this; profiling forwards always
+    // launch kernels individually).
     rfdetr_status enqueue(int batch, const uint8_t* d_src_rgb, int src_w, int src_h);
     // Synchronize the stream and check the device error word.
     rfdetr_status finish();
@@ -77,6 +81,16 @@ public:
 
 private:
     Engine() = default;
+    rfdetr_status enqueue_raw(int batch, const uint8_t* d_src_rgb, int src_w, int src_h);
+    void drop_graphs();
+    struct GraphEntry {
+        int batch;
+        const uint8_t* src;
+        int w, h;
+        cudaGraphExec_t exec;
+    };
+    std::vector<GraphEntry> graphs_;
+    bool use_graphs_ = true;
     rfdetr_status upload_weights(const Model& m);
     rfdetr_status alloc_activations(int batch);
     void free_activations();

@@ -83,48 +83,56 @@ __global__ void k_patch_im2col(const float* __restrict__ img, int B, int S, int 
 // Preprocess (src/image_io.cpp:207-248) fused into the patch im2col: each
 // im2col element is one normalized model-resolution pixel, sampled straight
 // from the uint8 source with the same double-precision source coordinates.
+// One thread per (patch, channel, kernel row): p consecutive outputs, so the
+// index arithmetic is paid once per p elements.
 __global__ void k_patch_from_rgb(const uint8_t* __restrict__ rgb, int B, int w, int h, int S, int p, int nw, int Kpad,
                                  float m0, float m1, float m2, float s0, float s1, float s2, __half* __restrict__ A) {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int G = S / p, ws = G / nw, Tp = ws * ws;
+    const int segs = 3 * p;  // (channel, ky) segments per patch
     const size_t rows = (size_t)B * nw * nw * Tp;
-    if (i >= rows * Kpad) return;
-    const size_t row = i / Kpad;
-    const int k = (int)(i - row * Kpad);
-    float v = 0.f;
-    if (k < 3 * p * p) {
-        const int b = (int)(row / ((size_t)nw * nw * Tp));
-        const int rr = (int)(row - (size_t)b * nw * nw * Tp);
-        const int win = rr / Tp, t = rr - win * Tp;
-        const int gy = (win / nw) * ws + t / ws, gx = (win % nw) * ws + t % ws;
-        const int c = k / (p * p), ky = (k / p) % p, kx = k % p;
-        const int yy = gy * p + ky, xx = gx * p + kx;
-        const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2), sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
-        if (w == S && h == S) {
-            // identity resize: source coordinate == destination, interpolation weights 0
-            const float px = (float)rgb[(((size_t)b * h + yy) * w + xx) * 3 + c];
-            A[i] = __float2half_rn((px / 255.0f - mean) / sd);
-            return;
-        }
-        const double scx = (double)w / (double)S, scy = (double)h / (double)S;
-        const double fy = ((double)yy + 0.5) * scy - 0.5;
-        const int y0r = (int)floor(fy);
-        const int y0 = min(max(y0r, 0), h - 1), y1 = min(max(y0r + 1, 0), h - 1);
-        const float wy = (float)(fy - (double)y0r);
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * segs + rows) return;
+    if (i >= rows * segs) {  // zero the K padding of one row
+        const size_t row = i - rows * segs;
+        for (int k = 3 * p * p; k < Kpad; ++k) A[row * Kpad + k] = __float2half_rn(0.f);
+        return;
+    }
+    const size_t row = i / segs;
+    const int seg = (int)(i - row * segs);
+    const int c = seg / p, ky = seg - c * p;
+    const int b = (int)(row / ((size_t)nw * nw * Tp));
+    const int rr = (int)(row - (size_t)b * nw * nw * Tp);
+    const int win = rr / Tp, t = rr - win * Tp;
+    const int gy = (win / nw) * ws + t / ws, gx = (win % nw) * ws + t % ws;
+    const int yy = gy * p + ky, x0p = gx * p;
+    const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2), sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+    const uint8_t* img = rgb + (size_t)b * h * w * 3;
+    __half* dst = A + row * Kpad + (size_t)(c * p + ky) * p;
+    if (w == S && h == S) {
+        // identity resize: source coordinate == destination, interpolation weights 0
+        const uint8_t* src = img + ((size_t)yy * w + x0p) * 3 + c;
+        for (int kx = 0; kx < p; ++kx) dst[kx] = __float2half_rn(((float)src[kx * 3] / 255.0f - mean) / sd);
+        return;
+    }
+    const double scx = (double)w / (double)S, scy = (double)h / (double)S;
+    const double fy = ((double)yy + 0.5) * scy - 0.5;
+    const int y0r = (int)floor(fy);
+    const int y0 = min(max(y0r, 0), h - 1), y1 = min(max(y0r + 1, 0), h - 1);
+    const float wy = (float)(fy - (double)y0r);
+    for (int kx = 0; kx < p; ++kx) {
+        const int xx = x0p + kx;
         const double fx = ((double)xx + 0.5) * scx - 0.5;
         const int x0r = (int)floor(fx);
         const int x0 = min(max(x0r, 0), w - 1), x1 = min(max(x0r + 1, 0), w - 1);
         const float wx = (float)(fx - (double)x0r);
-        const uint8_t* img = rgb + (size_t)b * h * w * 3;
         const float p00 = (float)img[((size_t)y0 * w + x0) * 3 + c];
         const float p01 = (float)img[((size_t)y0 * w + x1) * 3 + c];
         const float p10 = (float)img[((size_t)y1 * w + x0) * 3 + c];
         const float p11 = (float)img[((size_t)y1 * w + x1) * 3 + c];
         const float top = p00 + (p01 - p00) * wx;
         const float bot = p10 + (p11 - p10) * wx;
-        v = ((top + (bot - top) * wy) / 255.0f - mean) / sd;
+        dst[kx] = __float2half_rn(((top + (bot - top) * wy) / 255.0f - mean) / sd);
     }
-    A[i] = __float2half_rn(v);
 }
 
 __global__ void k_cls_rows(float* __restrict__ x, const float* __restrict__ clsrow, int B, int NW, int T, int D) {
@@ -568,7 +576,8 @@ cudaError_t patch_im2col(const float* img, int B, int S, int p, int nw, int Kpad
 cudaError_t patch_from_rgb(const uint8_t* rgb, int B, int w, int h, int S, int p, int nw, int Kpad,
                            const float* mean3, const float* std3, __half* A, cudaStream_t st) {
     const int G = S / p, Tp = (G / nw) * (G / nw);
-    const size_t n = (size_t)B * nw * nw * Tp * Kpad;
+    const size_t rows = (size_t)B * nw * nw * Tp;
+    const size_t n = rows * 3 * p + rows;
     k_patch_from_rgb<<<cdiv(n, 256), 256, 0, st>>>(rgb, B, w, h, S, p, nw, Kpad, mean3[0], mean3[1], mean3[2],
                                                    std3[0], std3[1], std3[2], A);
     return cudaGetLastError();

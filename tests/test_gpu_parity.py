@@ -123,3 +123,26 @@ def test_nano_batch1_parity(make_model):
     assert rel(lg[0], forced["logits"]) < 1e-3
     assert rel(bx[0], forced["boxes"]) < 1e-3
     eng.close()
+
+
+def test_graph_replay_matches_direct_launches(make_model, monkeypatch):
+    """The second and later forwards of a shape replay a captured CUDA graph;
+    they must reproduce the directly launched forward bit for bit."""
+    from rfdetr_b200 import lib
+
+    path = make_model("tiny", "f16", 0)
+    S = 128
+    a, b = _images(S, 2, 21), _images(S, 2, 22)
+    eng = lib.Engine(path, max_batch=2)
+    la1, ba1, _ = eng.forward_rgb(a)      # direct launches (+ capture)
+    lb_graph, bb_graph, _ = eng.forward_rgb(b)  # graph replay, new input
+    la2, ba2, _ = eng.forward_rgb(a)      # graph replay again
+    eng.close()
+    assert np.array_equal(la1, la2) and np.array_equal(ba1, ba2)
+    monkeypatch.setenv("RFDETR_NO_GRAPH", "1")
+    direct = lib.Engine(path, max_batch=2)
+    lb_direct, bb_direct, _ = direct.forward_rgb(b)
+    lb_direct2, _, _ = direct.forward_rgb(b)
+    direct.close()
+    assert np.array_equal(lb_graph, lb_direct) and np.array_equal(bb_graph, bb_direct)
+    assert np.array_equal(lb_direct, lb_direct2)
