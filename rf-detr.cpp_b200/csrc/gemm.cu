@@ -30,11 +30,11 @@ constexpr int BK = 64;
 
 template <int BN>
 struct Cfg {
-    static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr int STAGES = BN >= 192 ? 4 : (BN == 128 ? 6 : 8);
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int TMEM_COLS = BN == 192 ? 512 : 2 * BN;  // power of two >= 2 * BN
     static constexpr int OUT_STAGE = 8 * 4096;  // per epilogue warp: one 32-row x 128-byte box
     static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -237,9 +237,10 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         uint8_t* wptr = out_stage + quad * 8192 + half * 4096;
         const uint32_t wbuf = smem_u32(wptr);
         constexpr bool kSplit = (EPI != EPI_LN) && (BN >= 128);
+        constexpr int kHalf0 = ((BN / 2 + 63) / 64) * 64;  // first half: whole 64-column chunks
         const bool active = kSplit || half == 0;
-        const int col_begin = kSplit ? half * (BN / 2) : 0;
-        const int col_end = kSplit ? col_begin + BN / 2 : BN;
+        const int col_begin = kSplit ? half * kHalf0 : 0;
+        const int col_end = kSplit ? (half ? BN : kHalf0) : BN;
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int b = tile / tiles_per_batch;
@@ -530,6 +531,7 @@ template <int EPI, int ACT>
 cudaError_t dispatch_bn(const GemmArgs& a, int bn, cudaStream_t st) {
     switch (bn) {
         case 256: return launch<256, EPI, ACT>(a, st);
+        case 192: return launch<192, EPI, ACT>(a, st);
         case 128: return launch<128, EPI, ACT>(a, st);
         default: return launch<64, EPI, ACT>(a, st);
     }
@@ -551,6 +553,8 @@ cudaError_t gemm(const GemmArgs& a, cudaStream_t stream) {
         bn = a.N;
     } else if (a.N % 256 == 0) {
         bn = 256;
+    } else if (a.N % 192 == 0) {
+        bn = 192;  // N = 384 / 1152: two or six 192-wide tiles instead of 128-wide ones
     } else if (a.N > 64) {
         bn = 128;
     } else {
