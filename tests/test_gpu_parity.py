@@ -146,3 +146,161 @@ def test_graph_replay_matches_direct_launches(make_model, monkeypatch):
     direct.close()
     assert np.array_equal(lb_graph, lb_direct) and np.array_equal(bb_graph, bb_direct)
     assert np.array_equal(lb_direct, lb_direct2)
+
+
+# Every configuration the benchmark description names, at its real model size
+# (batch 2: the oracle checks both images; the full batches run through the
+# same kernels, only more rows).
+FULL = [("nano", "f16"), ("base", "q8_0"), ("medium", "q4_K"), ("seg-small", "f16"), ("large", "f16")]
+
+
+@pytest.mark.parametrize("variant,dtype", FULL)
+def test_full_size_configs(variant, dtype, make_model):
+    import oracle as O
+    from rfdetr_b200 import lib
+
+    path = make_model(variant, dtype, 0)
+    ora = O.Oracle(path)
+    eng = lib.Engine(path, max_batch=2)
+    S = eng.image_size
+    imgs = _images(S, 2, 500 + S)
+    lg, bx, mk = eng.forward_rgb(imgs)
+    NQ, NC = eng.nq, eng.nc
+    G = S // int(ora.meta["rfdetr.patch_size"])
+    topk = eng.trace("topk", 2).reshape(2, NQ).astype(np.int64)
+    cls_gpu = eng.trace("two_stage.cls_all", 2).reshape(2, G * G, NC)
+    eng.close()
+    tol = TOL[dtype]
+    for b in range(2):
+        x = ora.preprocess(imgs[b])
+        own = ora.forward(x, trace=True)
+        cls_o = own["trace"]["two_stage.cls_all"].reshape(G * G, NC)
+        assert rel(cls_gpu[b], cls_o) < 3 * tol
+        check_topk(topk[b], own["topk"], cls_o.max(1), tol)
+        forced = ora.forward(x, force_topk=topk[b])
+        assert rel(lg[b], forced["logits"]) < tol, (variant, b, rel(lg[b], forced["logits"]))
+        assert rel(bx[b], forced["boxes"]) < tol, (variant, b)
+        if mk is not None:
+            assert ((mk[b] > 0) == (forced["masks"] > 0)).mean() >= 0.99
+
+
+def test_batch_position_invariance(make_model):
+    """An image's outputs do not depend on its position in the batch or on the
+    other images of the batch."""
+    from rfdetr_b200 import lib
+
+    path = make_model("tiny-base", "f16", 0)
+    eng = lib.Engine(path, max_batch=4)
+    imgs = _images(eng.image_size, 4, 77)
+    lg, bx, _ = eng.forward_rgb(imgs)
+    perm = imgs[[2, 0, 3, 1]]
+    lg2, bx2, _ = eng.forward_rgb(perm)
+    one, bone, _ = eng.forward_rgb(imgs[3:4])
+    eng.close()
+    assert np.array_equal(lg[[2, 0, 3, 1]], lg2) and np.array_equal(bx[[2, 0, 3, 1]], bx2)
+    assert np.array_equal(lg[3], one[0]) and np.array_equal(bx[3], bone[0])
+
+
+@pytest.mark.parametrize("src", [(100, 90), (300, 257), (128, 128)])
+def test_resize_path_matches_oracle_preprocess(src, make_model):
+    """Images not at the model resolution are resized on the GPU exactly like
+    rfdetr_preprocess (bilinear, half-pixel, double coordinates)."""
+    import oracle as O
+    from rfdetr_b200 import lib
+
+    path = make_model("tiny", "f32", 0)
+    ora = O.Oracle(path)
+    eng = lib.Engine(path)
+    w, h = src
+    img = np.random.default_rng(w + h).integers(0, 256, (1, h, w, 3), dtype=np.uint8)
+    lg, bx, _ = eng.forward_rgb(img)
+    lg2, bx2, _ = eng.forward_planar(ora.preprocess(img[0]))
+    eng.close()
+    assert rel(lg, lg2) < 1e-5 and rel(bx, bx2) < 1e-5
+
+
+def test_detect_api_matches_oracle_selection(make_model):
+    """rfdetr_detect end to end (C ABI): same detections as the oracle's
+    postprocess of the engine's raw outputs (src/postprocess.cpp rules)."""
+    import ctypes as C
+
+    import oracle as O
+    from rfdetr_b200 import lib
+
+    path = make_model("tiny", "f16", 0)
+    L = lib.lib()
+    st = C.c_int(0)
+    p = lib.Params(path.encode(), 1, lib.LOG_CB(), None)
+    ctx = L.rfdetr_init(C.byref(p), C.byref(st))
+    assert ctx and st.value == 0
+    assert L.rfdetr_context_num_queries(ctx) == 40 and L.rfdetr_context_image_size(ctx) == 128
+    img_np = np.random.default_rng(9).integers(0, 256, (200, 160, 3), dtype=np.uint8)
+    img = L.rfdetr_image_from_rgb_buffer(img_np.ctypes.data, 160, 200, C.byref(st))
+    dp = lib.DetectParams(0.5, 10, None, 0)
+    out = C.POINTER(lib.Detection)()
+    n = C.c_size_t(0)
+    assert L.rfdetr_detect(ctx, img, C.byref(dp), C.byref(out), C.byref(n)) == 0
+    dets = [(out[i].class_id, out[i].score, out[i].x1, out[i].y1, out[i].x2, out[i].y2, out[i].class_name)
+            for i in range(n.value)]
+    L.rfdetr_detections_free(out, n)
+    L.rfdetr_image_free(img)
+    L.rfdetr_free(ctx)
+    eng = lib.Engine(path)
+    lg, bx, _ = eng.forward_rgb(img_np[None])
+    eng.close()
+    q, c, s, xy = O.select(lg[0], bx[0], 0.5, 10, 160, 200)
+    assert len(dets) == len(q) and len(dets) > 0
+    for d, ci, si, box in zip(dets, c, s, xy):
+        assert d[0] == ci and abs(d[1] - si) < 1e-6
+        assert np.allclose(d[2:6], box, atol=1e-3)
+        assert d[6] is not None
+
+
+def test_flat_capi_with_png_and_seg_masks(make_model, tmp_path):
+    """LocalAI's flat API (rfdetr_capi_*) on a segmentation model: JSON
+    envelope, accessors, two-call sizing, PNG masks at the image size, and
+    clearing of the previous batch on a failed detect (tests/test_capi_flat.cpp,
+    tests/test_capi_accessors.cpp)."""
+    import ctypes as C
+    import json
+    import struct
+    import zlib
+
+    from rfdetr_b200 import lib
+
+    path = make_model("seg-tiny", "f16", 0)
+    L = lib.lib()
+    h = C.c_size_t(0)
+    assert L.rfdetr_capi_load(path.encode(), 1, C.byref(h)) == 0 and h.value
+    rgb = np.random.default_rng(3).integers(0, 256, (64, 80, 3), dtype=np.uint8)
+    rows = b"".join(b"\x00" + rgb[y].tobytes() for y in range(64))
+
+    def chunk(t, d):
+        return struct.pack(">I", len(d)) + t + d + struct.pack(">I", zlib.crc32(t + d) & 0xFFFFFFFF)
+    png = (b"\x89PNG\r\n\x1a\n" + chunk(b"IHDR", struct.pack(">IIBBBBB", 80, 64, 8, 2, 0, 0, 0)) +
+           chunk(b"IDAT", zlib.compress(rows)) + chunk(b"IEND", b""))
+    out = C.c_void_p()
+    assert L.rfdetr_capi_detect_buffer(h, png, len(png), 0.3, 5, C.byref(out)) == 0
+    js = json.loads(C.string_at(out).decode())
+    L.rfdetr_capi_free_string(out)
+    assert js["status"] == "ok" and js["image"] == {"width": 80, "height": 64}
+    n = L.rfdetr_capi_get_n_detections(h)
+    assert n == len(js["detections"]) and 0 < n <= 5
+    xy = (C.c_float * 4)()
+    for i in range(n):
+        assert L.rfdetr_capi_get_detection_box(h, i, xy) == 0
+        assert abs(xy[0] - js["detections"][i]["x1"]) < 1e-2
+        need = L.rfdetr_capi_get_detection_class_name(h, i, None, 0)
+        buf = C.create_string_buffer(need)
+        assert L.rfdetr_capi_get_detection_class_name(h, i, buf, need) == need
+        msz = L.rfdetr_capi_get_detection_mask_png(h, i, None, 0)
+        assert msz > 0
+        mbuf = (C.c_ubyte * msz)()
+        assert L.rfdetr_capi_get_detection_mask_png(h, i, mbuf, msz) == msz
+        mp = bytes(mbuf)
+        assert mp[:8] == b"\x89PNG\r\n\x1a\n" and struct.unpack(">II", mp[16:24]) == (80, 64)
+    assert L.rfdetr_capi_get_detection_class_id(h, n) == -1
+    # a failed detect clears the previous batch
+    assert L.rfdetr_capi_detect_buffer(h, b"not an image", 12, 0.3, 5, C.byref(out)) != 0
+    assert L.rfdetr_capi_get_n_detections(h) == 0
+    assert L.rfdetr_capi_unload(h) == 0
