@@ -104,8 +104,11 @@ int rfdetr_b200_dequantize(uint32_t ggml_type, const void* src, long long n, flo
  * GEMM: out = epilogue(A[M][K] . B[N][K]^T + bias) with f16 A / B (K
  * contiguous, lda/ldb multiples of 8) and f32 accumulation on the tcgen05
  * tensor cores.  epi: 0 f16 out, 1 f32 out, 2 f32 out += colscale * value,
- * 4 full-row LayerNorm (N = 128 or 256) -> f32 and/or f16.  act: 0 none,
- * 1 GELU (erf), 2 ReLU, 3 SiLU. */
+ * 4 full-row LayerNorm of x = colscale * value + resid (N = 128, 256 or 384;
+ * colscale and resid optional) -> f32 and/or f16, 5 residual update fused
+ * with the LayerNorm that follows it: out32 = resid + colscale * value (out32
+ * may alias resid) and out16 = LayerNorm(out32) (N = 128, 256 or 384, act 0).
+ * value = acc + bias.  act: 0 none, 1 GELU (erf), 2 ReLU, 3 SiLU. */
 int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int epi, int act,
                         const float* bias, const float* colscale, const float* ln_g, const float* ln_b,
                         float ln_eps, const float* resid, int ldr, float* out32, int ld32, void* out16, int ld16,

@@ -14,7 +14,11 @@ enum GemmEpi : int {
     EPI_F32 = 1,    // out32 = act(acc + bias)
     EPI_RESID = 2,  // out32 += colscale * act(acc + bias)        (layer-scale + residual)
     EPI_PATCH = 3,  // patch embed: windowed row remap, + bias + windowed pos-embed -> out32
-    EPI_LN = 4,     // full-row LayerNorm(acc + bias [+ resid]) * g + b, act -> out32 / out16 (BN == N)
+    EPI_LN = 4,     // full-row LayerNorm(colscale * (acc + bias) [+ resid]) * g + b, act -> out32 / out16
+                    // (BN == N = 128, 256 or 384)
+    EPI_RESID_LN = 5,  // out32 = resid + colscale * (acc + bias) (may alias resid; the residual stream
+                       // update) and out16 = LayerNorm(out32) * g + b: a residual GEMM fused with the
+                       // LayerNorm that reads its result
 };
 
 enum GemmAct : int { ACT_NONE = 0, ACT_GELU = 1, ACT_RELU = 2, ACT_SILU = 3 };
@@ -50,6 +54,7 @@ struct GemmArgs {
     int patch_rows = 0;    // patch rows per image
     int patch_ntok = 0;    // tokens per image
     const float* posw = nullptr;  // [ntok][N] windowed pos-embed
+    int ln_pre32 = 0;      // EPI_LN: out32 receives the sum before normalisation (set for EPI_RESID_LN)
     int* err = nullptr;    // device error word
     int tma_out = 0;       // set by the launcher: outputs written through TMA stores
 };

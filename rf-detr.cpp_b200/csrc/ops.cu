@@ -8,7 +8,8 @@ extern "C" int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ld
                                    int act, const float* bias, const float* colscale, const float* ln_g,
                                    const float* ln_b, float ln_eps, const float* resid, int ldr, float* out32,
                                    int ld32, void* out16, int ld16, void* stream) {
-    if (epi != rfb::EPI_F16 && epi != rfb::EPI_F32 && epi != rfb::EPI_RESID && epi != rfb::EPI_LN)
+    if (epi != rfb::EPI_F16 && epi != rfb::EPI_F32 && epi != rfb::EPI_RESID && epi != rfb::EPI_LN &&
+        epi != rfb::EPI_RESID_LN)
         return (int)cudaErrorInvalidValue;
     if ((epi == rfb::EPI_F16 && !out16) || ((epi == rfb::EPI_F32 || epi == rfb::EPI_RESID) && !out32))
         return (int)cudaErrorInvalidValue;

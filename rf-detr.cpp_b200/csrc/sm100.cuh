@@ -107,6 +107,11 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const 
 }
 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Bring `bytes` (multiple of 16) of global memory at `p` (16-byte aligned)
+// into L2, asynchronously; nothing to wait for.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 // Wait until at most N committed bulk groups still read shared memory.
 template <int N>
 __device__ __forceinline__ void bulk_wait_read() {

@@ -2,11 +2,14 @@
 
     python -m rfdetr_b200.kernels_bench gemm --m 51712 --n 1536 --k 384 [--epi 0 --act 1]
     python -m rfdetr_b200.kernels_bench attn --seq 1616 --groups 32 --heads 6 --hd 64
+    python -m rfdetr_b200.kernels_bench deform --batch 32 --grid 40 --nq 300 --heads 16 --points 2
 
 Times `--iters` launches with CUDA events on the current stream (after
 `--warmup` launches) and prints one JSON line: ms per launch and achieved
 TFLOP/s (algorithmic FLOPs: 2*M*N*K for a GEMM, 4*L^2*hd per (group, head)
-for attention).  Used for ncu captures of one kernel in isolation.
+for attention) or GB/s for the deformable sampling (algorithmic bytes: the
+value map read once, the offset/logit rows, the reference points and the f16
+output).  Used for ncu captures of one kernel in isolation.
 """
 import argparse
 import json
@@ -19,7 +22,7 @@ from . import lib
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "attn"])
+    ap.add_argument("op", choices=["gemm", "attn", "deform"])
     ap.add_argument("--m", type=int, default=51712)
     ap.add_argument("--n", type=int, default=1536)
     ap.add_argument("--k", type=int, default=384)
@@ -29,6 +32,11 @@ def main():
     ap.add_argument("--groups", type=int, default=32)
     ap.add_argument("--heads", type=int, default=6)
     ap.add_argument("--hd", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--grid", type=int, default=40)
+    ap.add_argument("--nq", type=int, default=300)
+    ap.add_argument("--points", type=int, default=2)
+    ap.add_argument("--dm", type=int, default=256)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
@@ -51,6 +59,20 @@ def main():
             assert rc == 0, rc
         flops = 2.0 * a.m * a.n * a.k
         name = f"gemm M={a.m} N={a.n} K={a.k} epi={a.epi} act={a.act}"
+    elif a.op == "deform":
+        H, P, Dm, NQ, G, B = a.heads, a.points, a.dm, a.nq, a.grid, a.batch
+        ld = H * P * 3
+        value = (torch.randn(B * G * G, Dm, device=dev, generator=g)).half()
+        so_aw = torch.randn(B * NQ, ld, device=dev, generator=g)
+        refp = torch.rand(B * NQ, 4, device=dev, generator=g) * 0.5 + 0.25
+        out = torch.empty(B * NQ, Dm, dtype=torch.float16, device=dev)
+
+        def run():
+            rc = L.rfdetr_b200_op_deform(value.data_ptr(), so_aw.data_ptr(), ld, refp.data_ptr(), B, NQ, G, H, P,
+                                         Dm, out.data_ptr(), st)
+            assert rc == 0, rc
+        nbytes = value.numel() * 2 + so_aw.numel() * 4 + refp.numel() * 4 + out.numel() * 2
+        name = f"deform batch={B} grid={G} nq={NQ} heads={H} points={P} dm={Dm}"
     else:
         D = a.heads * a.hd
         qkv = torch.randn(a.groups * a.seq, 3 * D, device=dev, generator=g).half()
@@ -73,7 +95,11 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.iters
-    print(json.dumps({"op": name, "ms": round(ms, 5), "tflops": round(flops / ms / 1e9, 1)}))
+    if a.op == "deform":
+        print(json.dumps({"op": name, "ms": round(ms, 5), "gbs": round(nbytes / ms / 1e6, 1),
+                          "bytes": nbytes}))
+    else:
+        print(json.dumps({"op": name, "ms": round(ms, 5), "tflops": round(flops / ms / 1e9, 1)}))
 
 
 if __name__ == "__main__":

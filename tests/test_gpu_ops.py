@@ -69,12 +69,15 @@ def test_gemm(M, N, K, epi, act):
         assert rel(out32, base.double() + scale.double() * ref) < 1e-4
 
 
-@pytest.mark.parametrize("N", [128, 256])
+@pytest.mark.parametrize("N", [128, 256, 384])
 @pytest.mark.parametrize("act,with_resid", [(0, True), (3, False)])
-def test_gemm_layernorm_epilogue(N, act, with_resid):
+@pytest.mark.parametrize("M", [777, 40000])
+def test_gemm_layernorm_epilogue(N, act, with_resid, M):
+    if N == 384 and act == 3:
+        pytest.skip("SiLU is instantiated for the 128 / 256-wide projector LayerNorms only")
     torch.manual_seed(N + act)
     dev = "cuda:0"
-    M, K = 777, 640
+    K = 640
     A = torch.randn(M, K, device=dev).half()
     B = (torch.randn(N, K, device=dev) * 0.05).half()
     bias = torch.randn(N, device=dev) * 0.1
@@ -94,6 +97,36 @@ def test_gemm_layernorm_epilogue(N, act, with_resid):
     assert rc == 0
     torch.cuda.synchronize()
     assert rel(out32, ref) < 1e-4
+    assert rel(out16, ref) < 2e-3
+
+
+@pytest.mark.parametrize("N", [128, 256, 384])
+@pytest.mark.parametrize("M,K", [(777, 384), (40000, 1536)])
+@pytest.mark.parametrize("pitch", [0, 1])
+def test_gemm_residual_layernorm_fused(N, M, K, pitch):
+    """epi 5: x = resid + colscale * (A.B^T + bias) written over resid, LN(x) -> out16.
+
+    pitch = 1 pads the f32 rows by one element (not a multiple of 16 bytes), which
+    routes the stores through the direct-store path instead of TMA.
+    """
+    torch.manual_seed(N + M + pitch)
+    dev = "cuda:0"
+    ld = N + pitch
+    A = torch.randn(M, K, device=dev).half()
+    B = (torch.randn(N, K, device=dev) * 0.05).half()
+    bias = torch.randn(N, device=dev) * 0.1
+    scale = torch.rand(N, device=dev) + 0.5
+    g = torch.rand(N, device=dev) + 0.5
+    b = torch.randn(N, device=dev) * 0.1
+    x = torch.randn(M, ld, device=dev) * 2.0 + 0.3
+    x_ref = x[:, :N].double() + scale.double() * (A.double() @ B.double().T + bias.double())
+    ref = F.layer_norm(x_ref, (N,), g.double(), b.double(), 1e-6)
+    out16 = torch.zeros(M, N, dtype=torch.float16, device=dev)
+    rc = _lib().rfdetr_b200_op_gemm(_p(A), K, _p(B), K, M, N, K, 5, 0, _p(bias), _p(scale), _p(g), _p(b), 1e-6,
+                                    _p(x), ld, _p(x), ld, _p(out16), N, _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert rel(x[:, :N], x_ref) < 1e-5
     assert rel(out16, ref) < 2e-3
 
 
