@@ -2,7 +2,7 @@
 // the windowed and global blocks of the DINOv2 backbone.
 //
 // One CTA = 128 query rows of one (group, head); keys in blocks of 64.
-//   warp 0      TMA: Q once, then K/V blocks into a 2-slot ring (3-D tensor
+//   warp 0      TMA: Q once, then K/V blocks into a 4-slot ring (3-D tensor
 //               maps (column, token, group): rows past the sequence end load
 //               as zeros)
 //   warp 1      TMEM allocation; one lane issues tcgen05.mma:
@@ -10,7 +10,10 @@
 //                 O += P V             (M=128, N=64,  K=64)  -> TMEM cols [64, 128)
 //               S of block j+1 is issued as soon as the softmax has read S_j.
 //   warps 2..5  one thread per query row: read S_j from TMEM, online softmax in
-//               f32 (exp2 domain), rescale O in TMEM when the row max moves,
+//               f32 (exp2 domain); the reference max is only raised (and O in
+//               TMEM rescaled) when a row's max grows by more than 2^8, so P
+//               stays <= 256 and the rescale is rare (the result is the same
+//               softmax: numerator and denominator share the reference);
 //               write P_j (f16) into 128B-swizzled shared memory as the A
 //               operand of the P V product; at the end O / l -> f16 -> TMA store
 //               (3-D map clips rows past the sequence end).
@@ -36,7 +39,9 @@ constexpr int HD = 64;                  // head dim
 constexpr int Q_BYTES = AQ * HD * 2;    // 16 KB
 constexpr int KV_BYTES = AK * HD * 2;   // 8 KB
 constexpr int P_BYTES = AQ * AK * 2;    // 16 KB
-constexpr int SMEM_TILES = Q_BYTES + 4 * KV_BYTES + P_BYTES;  // 64 KB
+constexpr int NS = 4;                   // K/V ring slots (prefetch depth)
+constexpr int SMEM_TILES = Q_BYTES + 2 * NS * KV_BYTES + P_BYTES;  // 96 KB
+constexpr float kRescaleLog2 = 8.0f;    // lazy rescale threshold (log2 units)
 constexpr int SMEM = SMEM_TILES + 1024 + 256;
 constexpr int TMEM_COLS = 128;          // S: [0,64), O: [64,128)
 
@@ -62,18 +67,18 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
-    uint8_t* sK = sQ + Q_BYTES;            // 2 slots
-    uint8_t* sV = sK + 2 * KV_BYTES;       // 2 slots
-    uint8_t* sP = sV + 2 * KV_BYTES;
+    uint8_t* sK = sQ + Q_BYTES;            // NS slots
+    uint8_t* sV = sK + NS * KV_BYTES;      // NS slots
+    uint8_t* sP = sV + NS * KV_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_TILES);
     uint64_t* q_full = bars + 0;
-    uint64_t* kv_full = bars + 1;   // [2]
-    uint64_t* kv_empty = bars + 3;  // [2]
-    uint64_t* s_full = bars + 5;
-    uint64_t* s_free = bars + 6;
-    uint64_t* p_full = bars + 7;
-    uint64_t* pv_done = bars + 8;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 9);
+    uint64_t* kv_full = bars + 1;        // [NS]
+    uint64_t* kv_empty = bars + 1 + NS;  // [NS]
+    uint64_t* s_full = bars + 1 + 2 * NS;
+    uint64_t* s_free = s_full + 1;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* pv_done = s_full + 3;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_full + 4);
     volatile int* cta_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -84,10 +89,10 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        mbar_init(&kv_full[0], 1);
-        mbar_init(&kv_full[1], 1);
-        mbar_init(&kv_empty[0], 1);
-        mbar_init(&kv_empty[1], 1);
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+        }
         mbar_init(s_full, 1);
         mbar_init(s_free, 128);
         mbar_init(p_full, 128);
@@ -110,8 +115,8 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             mbar_arrive_expect_tx(q_full, Q_BYTES);
             tma_load_3d(&tmQ, q_full, sQ, head * HD, q0, g);
             for (int j = 0; j < nb; ++j) {
-                const int slot = j & 1;
-                if (!mbar_wait(&kv_empty[slot], ((j >> 1) & 1) ^ 1, cta_abort, err)) break;
+                const int slot = j % NS;
+                if (!mbar_wait(&kv_empty[slot], ((j / NS) & 1) ^ 1, cta_abort, err)) break;
                 mbar_arrive_expect_tx(&kv_full[slot], 2 * KV_BYTES);
                 tma_load_3d(&tmK, &kv_full[slot], sK + slot * KV_BYTES, head * HD, j * AK, g);
                 tma_load_3d(&tmV, &kv_full[slot], sV + slot * KV_BYTES, head * HD, j * AK, g);
@@ -132,11 +137,11 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
                 umma_commit(s_full);
             }
             for (int j = 0; ok && j < nb; ++j) {
-                const int slot = j & 1;
+                const int slot = j % NS;
                 if (j + 1 < nb) {
-                    const int ns = (j + 1) & 1;
+                    const int ns = (j + 1) % NS;
                     if (!mbar_wait(s_free, j & 1, cta_abort, err)) break;
-                    if (!mbar_wait(&kv_full[ns], ((j + 1) >> 1) & 1, cta_abort, err)) break;
+                    if (!mbar_wait(&kv_full[ns], ((j + 1) / NS) & 1, cta_abort, err)) break;
                     tc_fence_after();
                     const uint32_t k_s = smem_u32(sK + ns * KV_BYTES);
 #pragma unroll
@@ -175,7 +180,7 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             mbar_arrive(s_free);
             const int kbase = j * AK;
             const bool full_block = kbase + AK <= L;
-            float mx = -INFINITY;  // row max of raw scores (scale > 0 commutes with max)
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // row max of raw scores
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
                 float x0 = __uint_as_float(r0[e]), x1 = __uint_as_float(r1[e]);
@@ -185,20 +190,26 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
                     r0[e] = __float_as_uint(x0);
                     r1[e] = __float_as_uint(x1);
                 }
-                mx = fmaxf(mx, fmaxf(x0, x1));
+                mx4[e & 3] = fmaxf(mx4[e & 3], fmaxf(x0, x1));
             }
-            const float m_new = fmaxf(m, mx * sl2);  // running max in log2 units
-            const float alpha = ex2(m - m_new);      // 0 on the first block (m = -inf)
-            float rs = 0.f;
+            // scale > 0 commutes with max; running max in log2 units
+            const float m_cand = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2);
+            const float m_new = m_cand > m + kRescaleLog2 ? m_cand : m;  // always taken on the first block
+            const float alpha = ex2(m - m_new);  // 1 while the reference holds; 0 on the first block
+            float2 rs2 = make_float2(0.f, 0.f);
+            const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_new, -m_new);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const float p0 = ex2(fmaf(__uint_as_float(r0[e]), sl2, -m_new));
-                const float p1 = ex2(fmaf(__uint_as_float(r1[e]), sl2, -m_new));
-                r0[e] = __float_as_uint(p0);
-                r1[e] = __float_as_uint(p1);
-                rs += p0 + p1;
+            for (int e = 0; e < 32; e += 2) {
+                const float2 a = __ffma2_rn(make_float2(__uint_as_float(r0[e]), __uint_as_float(r0[e + 1])), sl2v, negm);
+                const float2 c = __ffma2_rn(make_float2(__uint_as_float(r1[e]), __uint_as_float(r1[e + 1])), sl2v, negm);
+                const float2 pa = make_float2(ex2(a.x), ex2(a.y)), pc = make_float2(ex2(c.x), ex2(c.y));
+                r0[e] = __float_as_uint(pa.x);
+                r0[e + 1] = __float_as_uint(pa.y);
+                r1[e] = __float_as_uint(pc.x);
+                r1[e + 1] = __float_as_uint(pc.y);
+                rs2 = __fadd2_rn(rs2, __fadd2_rn(pa, pc));
             }
-            l = l * alpha + rs;
+            l = l * alpha + (rs2.x + rs2.y);
             m = m_new;
             if (j > 0) {
                 // previous P V done: P buffer reusable, O stable for the rescale
@@ -223,7 +234,12 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
                         tmem_ld32(tO + lanebase + c, o);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        for (int e = 0; e < 32; e += 2) {
+                            const float2 y = __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])),
+                                                        make_float2(alpha, alpha));
+                            o[e] = __float_as_uint(y.x);
+                            o[e + 1] = __float_as_uint(y.y);
+                        }
                         tmem_st32(tO + lanebase + c, o);
                     }
                     tmem_wait_st();
