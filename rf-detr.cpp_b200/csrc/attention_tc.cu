@@ -39,11 +39,19 @@ constexpr int HD = 64;                  // head dim
 constexpr int Q_BYTES = AQ * HD * 2;    // 16 KB
 constexpr int KV_BYTES = AK * HD * 2;   // 8 KB
 constexpr int P_BYTES = AQ * AK * 2;    // 16 KB
-constexpr int NS = 4;                   // K/V ring slots (prefetch depth)
-constexpr int SMEM_TILES = Q_BYTES + 2 * NS * KV_BYTES + P_BYTES;  // 96 KB
 constexpr float kRescaleLog2 = 8.0f;    // lazy rescale threshold (log2 units)
-constexpr int SMEM = SMEM_TILES + 1024 + 256;
 constexpr int TMEM_COLS = 128;          // S: [0,64), O: [64,128)
+
+// NS = K/V ring slots (prefetch depth).  Sequences of at most two key blocks
+// (windows of up to 128 tokens, e.g. the 101-token windows of a 40 x 40
+// grid) use two slots, which keeps a CTA at 64 KB of shared memory and lets
+// three run per SM; longer ones use four (96 KB, two per SM).
+template <int NS>
+struct AttnCfg {
+    static constexpr int SMEM_TILES = Q_BYTES + 2 * NS * KV_BYTES + P_BYTES;
+    static constexpr int SMEM = SMEM_TILES + 1024 + 256;
+    static constexpr int MIN_CTAS = NS == 2 ? 3 : 2;
+};
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -60,7 +68,8 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__global__ void __launch_bounds__(192, 2)
+template <int NS>
+__global__ void __launch_bounds__(192, AttnCfg<NS>::MIN_CTAS)
 k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, int L, float sl2,
           int* err) {
@@ -70,7 +79,7 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     uint8_t* sK = sQ + Q_BYTES;            // NS slots
     uint8_t* sV = sK + NS * KV_BYTES;      // NS slots
     uint8_t* sP = sV + NS * KV_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_TILES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AttnCfg<NS>::SMEM_TILES);
     uint64_t* q_full = bars + 0;
     uint64_t* kv_full = bars + 1;        // [NS]
     uint64_t* kv_empty = bars + 1 + NS;  // [NS]
@@ -322,7 +331,9 @@ cudaError_t attention_tc(const __half* q, const __half* k, const __half* v, int 
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_set.load() & bit)) {
-        e = cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        e = cudaFuncSetAttribute(k_attn_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<2>::SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_attn_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<4>::SMEM);
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
@@ -332,7 +343,11 @@ cudaError_t attention_tc(const __half* q, const __half* k, const __half* v, int 
         !make_seq_map(&mv, v, cols, seq_len, groups, ldv, AK) || !make_seq_map(&mo, o, cols, seq_len, groups, ldo, 32))
         return cudaErrorInvalidValue;
     const dim3 grid((seq_len + AQ - 1) / AQ, heads, groups);
-    k_attn_tc<<<grid, 192, SMEM, st>>>(mq, mk, mv, mo, seq_len, scale * 1.4426950408889634f, err);
+    const float sl2 = scale * 1.4426950408889634f;
+    if (seq_len <= 2 * AK)
+        k_attn_tc<2><<<grid, 192, AttnCfg<2>::SMEM, st>>>(mq, mk, mv, mo, seq_len, sl2, err);
+    else
+        k_attn_tc<4><<<grid, 192, AttnCfg<4>::SMEM, st>>>(mq, mk, mv, mo, seq_len, sl2, err);
     return cudaGetLastError();
 }
 

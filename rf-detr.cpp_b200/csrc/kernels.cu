@@ -180,46 +180,65 @@ __global__ void k_layernorm(const float* x, int rows, int D, const float* __rest
 }
 
 // Same, 16-byte vectors: lane owns columns 4*(lane + 32*i) .. +3, D = 128*NV.
+// Grid-stride over rows (one warp per row at a time); the next row's loads are
+// issued before the current row's reductions so each warp keeps two rows of
+// loads in flight.
 template <int NV>
-__global__ void k_layernorm_v4(const float* x, int rows, const float* __restrict__ g, const float* __restrict__ b,
-                               float eps, float* y32, __half* __restrict__ y16) {
+__global__ void __launch_bounds__(256) k_layernorm_v4(const float* x, int rows, const float* __restrict__ g,
+                                                     const float* __restrict__ b, float eps, float* y32,
+                                                     __half* __restrict__ y16) {
     constexpr int D = 128 * NV;
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    const int stride = gridDim.x * (blockDim.x >> 5);
+    int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
-    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * D);
+    float4 gg[NV], bb[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        gg[i] = *reinterpret_cast<const float4*>(g + 4 * (lane + 32 * i));
+        bb[i] = *reinterpret_cast<const float4*>(b + 4 * (lane + 32 * i));
+    }
     float4 v[NV];
-    float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        v[i] = xr[lane + 32 * i];
-        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-    }
-    const float mean = warp_sum(s) / (float)D;
-    float q = 0.f;
+    for (int i = 0; i < NV; ++i) v[i] = reinterpret_cast<const float4*>(x + (size_t)row * D)[lane + 32 * i];
+    for (; row < rows; row += stride) {
+        const int nxt = row + stride;
+        float4 vn[NV];
+        if (nxt < rows) {
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        const float a = v[i].x - mean, bq = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-        q += (a * a + bq * bq) + (c * c + d * d);
-    }
-    const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)D + eps);
+            for (int i = 0; i < NV; ++i) vn[i] = reinterpret_cast<const float4*>(x + (size_t)nxt * D)[lane + 32 * i];
+        }
+        float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        const int c0 = 4 * (lane + 32 * i);
-        const float4 gg = *reinterpret_cast<const float4*>(g + c0);
-        const float4 bb = *reinterpret_cast<const float4*>(b + c0);
-        float4 o;
-        o.x = (v[i].x - mean) * rstd * gg.x + bb.x;
-        o.y = (v[i].y - mean) * rstd * gg.y + bb.y;
-        o.z = (v[i].z - mean) * rstd * gg.z + bb.z;
-        o.w = (v[i].w - mean) * rstd * gg.w + bb.w;
-        if (y32) *reinterpret_cast<float4*>(y32 + (size_t)row * D + c0) = o;
-        if (y16) {
-            __half2 h0 = __floats2half2_rn(o.x, o.y), h1 = __floats2half2_rn(o.z, o.w);
-            uint2 u;
-            u.x = *reinterpret_cast<uint32_t*>(&h0);
-            u.y = *reinterpret_cast<uint32_t*>(&h1);
-            *reinterpret_cast<uint2*>(y16 + (size_t)row * D + c0) = u;
+        for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        const float mean = warp_sum(s) / (float)D;
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const float a = v[i].x - mean, bq = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+            q += (a * a + bq * bq) + (c * c + d * d);
+        }
+        const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)D + eps);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c0 = 4 * (lane + 32 * i);
+            float4 o;
+            o.x = (v[i].x - mean) * rstd * gg[i].x + bb[i].x;
+            o.y = (v[i].y - mean) * rstd * gg[i].y + bb[i].y;
+            o.z = (v[i].z - mean) * rstd * gg[i].z + bb[i].z;
+            o.w = (v[i].w - mean) * rstd * gg[i].w + bb[i].w;
+            if (y32) *reinterpret_cast<float4*>(y32 + (size_t)row * D + c0) = o;
+            if (y16) {
+                __half2 h0 = __floats2half2_rn(o.x, o.y), h1 = __floats2half2_rn(o.z, o.w);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t*>(&h0);
+                u.y = *reinterpret_cast<uint32_t*>(&h1);
+                *reinterpret_cast<uint2*>(y16 + (size_t)row * D + c0) = u;
+            }
+        }
+        if (nxt < rows) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) v[i] = vn[i];
         }
     }
 }
@@ -594,8 +613,10 @@ cudaError_t layernorm(const float* x, int rows, int D, const float* g, const flo
     if (D > 512) return cudaErrorInvalidValue;
     const unsigned blocks = cdiv(rows, 8);
     const bool vec = (D % 128 == 0) && !(((uintptr_t)x | (uintptr_t)y32 | (uintptr_t)y16) & 15);
-    if (vec && D == 384) k_layernorm_v4<3><<<blocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16);
-    else if (vec && D == 256) k_layernorm_v4<2><<<blocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16);
+    // the vector kernel is grid-strided: a few resident blocks per SM
+    const unsigned vblocks = blocks < (unsigned)(148 * 6) ? blocks : (unsigned)(148 * 6);
+    if (vec && D == 384) k_layernorm_v4<3><<<vblocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16);
+    else if (vec && D == 256) k_layernorm_v4<2><<<vblocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16);
     else if (D <= 256) k_layernorm<8><<<blocks, 256, 0, st>>>(x, rows, D, g, b, eps, y32, y16);
     else k_layernorm<16><<<blocks, 256, 0, st>>>(x, rows, D, g, b, eps, y32, y16);
     return cudaGetLastError();
