@@ -11,6 +11,8 @@ projector -> two-stage + top-K -> deformable decoder -> heads.
 
 N > 1 runs one process per GPU (torchrun); each rank processes its own batch
 (weak scaling, no collective on the data path); timing is the max over ranks.
+--global-batch B instead splits one batch of B images contiguously over the
+ranks (strong scaling).
 
 Reported (one JSON line on rank 0):
   value       images/s, inputs already resident in HBM (device pointer API)
@@ -49,22 +51,18 @@ def parse():
     p.add_argument("--variant", default=WORKLOAD["variant"])
     p.add_argument("--dtype", default=WORKLOAD["dtype"])
     p.add_argument("--batch", type=int, default=WORKLOAD["batch"])
+    p.add_argument("--global-batch", type=int, default=0,
+                   help="split this many images over the ranks (strong scaling) instead of --batch per rank")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
 
-def model_file(variant, dtype, rank, world, barrier):
+def model_file(variant, dtype, pg):
+    from rfdetr_b200 import replicas, synth
     d = os.environ.get("RFDETR_BENCH_DIR", os.path.join(tempfile.gettempdir(), "rfdetr_bench"))
     os.makedirs(d, exist_ok=True)
     path = os.path.join(d, f"{variant}-{dtype}-seed0.gguf")
-    if rank == 0 and not os.path.exists(path):
-        from rfdetr_b200 import synth
-        tmp = path + ".tmp"
-        synth.write_model(tmp, variant, dtype, 0)
-        os.replace(tmp, path)
-    if world > 1:
-        barrier()
-    return path
+    return replicas.create_once(path, lambda tmp: synth.write_model(tmp, variant, dtype, 0), pg)
 
 
 class Clocks:
@@ -176,7 +174,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    path = model_file(args.variant, args.dtype, 0, 1, None)
+    from rfdetr_b200 import replicas
+    path = model_file(args.variant, args.dtype, replicas.ProcessGroup(replicas.RankInfo()))
     cores = os.cpu_count() or 1
     cpu_oracle_run(path, max(args.warmup, 0), 7)
     n, dt = cpu_oracle_run(path, max(args.steps, 1), 11)
@@ -205,28 +204,29 @@ def main():
 
     import numpy as np
     import torch
-    import torch.distributed as dist
-    from rfdetr_b200 import lib, synth
+    from rfdetr_b200 import lib, replicas, synth
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    info = replicas.RankInfo.from_env()
+    rank, world, local = info.rank, info.world, info.local_rank
     torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    pg = replicas.ProcessGroup(info, "nccl", timeout_s=300.0, device=torch.device("cuda", local))
+    barrier = pg.barrier
 
     cfg = synth.get_variant(args.variant)
-    B, S = args.batch, cfg["image_size"]
-    path = model_file(args.variant, args.dtype, rank, world, barrier)
+    S = cfg["image_size"]
+    if args.global_batch > 0:
+        lo, hi = replicas.shard(args.global_batch, rank, world)
+        B, scaling, total = hi - lo, "strong", args.global_batch
+        if B == 0:
+            raise SystemExit("--global-batch smaller than the number of ranks")
+    else:
+        lo, B, scaling, total = rank * args.batch, args.batch, "weak", args.batch * world
+    path = model_file(args.variant, args.dtype, pg)
     eng = lib.Engine(path, device=local, max_batch=B)
     stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
-    rng = np.random.default_rng(1000 + rank)
-    imgs = rng.integers(0, 256, (B, S, S, 3), dtype=np.uint8)
+    # image i of the (global) batch is drawn from seed 1000 + i, whatever rank owns it
+    imgs = np.stack([np.random.default_rng(1000 + lo + i).integers(0, 256, (S, S, 3), dtype=np.uint8)
+                     for i in range(B)])
     d_imgs = torch.from_numpy(imgs).cuda(local)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local}")
     torch.cuda.synchronize()
@@ -252,11 +252,8 @@ def main():
         clk = clocks.stop()
         barrier()
     ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    t = torch.tensor([ms], device=f"cuda:{local}")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = B * world * args.steps / (ms_max / 1000.0)
+    ms_max = pg.max_over_ranks(ms)
+    value = total * args.steps / (ms_max / 1000.0)
     launches = eng.kernels_per_forward() * args.steps
 
     # ---- end to end through the C API (pinned host buffers) -------------
@@ -284,10 +281,7 @@ def main():
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    t = torch.tensor([e0.elapsed_time(e1)], device=f"cuda:{local}")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = B * world * args.steps / (float(t.item()) / 1000.0)
+    e2e_value = total * args.steps / (pg.max_over_ranks(e0.elapsed_time(e1)) / 1000.0)
     h2d = B * S * S * 3
     d2h = B * nq * (nc + 4) * 4
 
@@ -351,10 +345,10 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded uint8 images, seeded random-init weights)",
             "config": {"workload": f"RF-DETR {args.variant} {args.dtype}, batch {B} per GPU, {S}x{S} uint8 images",
-                       "global_batch": B * world, "per_gpu_batch": B, "image": S,
+                       "global_batch": total, "per_gpu_batch": B, "image": S,
                        "parallelism": f"dp{world} (independent replicas)",
                        "l2": "256 MB buffer written between timed steps (L2 is 126 MB)"},
             "e2e": {"value": round(e2e_value, 2), "unit": "images/s", "h2d_bytes_per_step": h2d,
@@ -375,9 +369,9 @@ def main():
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    pg.barrier()  # rank 0's latency / CPU legs are done before any rank tears down
     eng.close()
-    if world > 1:
-        dist.destroy_process_group()
+    pg.close()
     return 0
 
 
