@@ -150,18 +150,28 @@ def traffic_from_profiles():
         return None
 
 
-def cpu_oracle_run(path, n_images, seed, time_budget_s=None):
+def host_threads():
+    """Cores this process may run on (torchrun pins OMP_NUM_THREADS to 1 per
+    rank, so the CPU legs set their thread count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def cpu_oracle_run(path, n_images, seed, time_budget_s=None, threads=None):
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import numpy as np
     import oracle as O
     ora = O.Oracle(path)
     S = ora.image_size
     rng = np.random.default_rng(seed)
+    nt = threads or host_threads()
     done = 0
     t0 = time.perf_counter()
     while done < n_images:
         img = rng.integers(0, 256, (S, S, 3), dtype=np.uint8)
-        ora.forward(ora.preprocess(img))
+        ora.forward(ora.preprocess(img), n_threads=nt)
         done += 1
         if time_budget_s and time.perf_counter() - t0 > time_budget_s:
             break
@@ -176,9 +186,9 @@ def run_reference(args):
         return 0
     from rfdetr_b200 import replicas
     path = model_file(args.variant, args.dtype, replicas.ProcessGroup(replicas.RankInfo()))
-    cores = os.cpu_count() or 1
-    cpu_oracle_run(path, max(args.warmup, 0), 7)
-    n, dt = cpu_oracle_run(path, max(args.steps, 1), 11)
+    cores = host_threads()
+    cpu_oracle_run(path, max(args.warmup, 0), 7, threads=cores)
+    n, dt = cpu_oracle_run(path, max(args.steps, 1), 11, threads=cores)
     v = n / dt
     from rfdetr_b200 import synth
     cfg = synth.get_variant(args.variant)
@@ -335,8 +345,8 @@ def main():
     # ---- CPU baseline (rank 0, N = 1) ------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        n_img, dt = cpu_oracle_run(path, 8, 5, time_budget_s=20.0)
-        cores = os.cpu_count() or 1
+        cores = host_threads()
+        n_img, dt = cpu_oracle_run(path, 8, 5, time_budget_s=20.0, threads=cores)
         cpu = {"value": round(n_img / dt, 4), "unit": "images/s", "cores": cores, "kind": "port",
                "sample": f"{n_img} of the {B} images of one step, restated reference forward (f32), "
                          f"OpenMP over {cores} threads"}
