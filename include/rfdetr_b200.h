@@ -130,10 +130,13 @@ int rfdetr_b200_op_deform(const void* value, const float* so_aw, int ld_soaw, co
  * maps (`src` rows = batch*h*w pixels, `c` channels at pitch `lds`), followed
  * by a LayerNorm over the `oc` output channels (oc = 128 or 256) and an
  * optional activation (0 none, 3 SiLU): the projector's ConvX block
- * (src/projector.cpp:46-59).  weight is f16 [oc][3][3][c].  The convolution
- * runs as an im2col into `workspace` followed by a tcgen05 GEMM with the
- * LayerNorm fused into its epilogue; workspace must hold
- * rfdetr_b200_op_conv3x3_workspace(batch, h, w, c) bytes of device memory. */
+ * (src/projector.cpp:46-59).  weight is f16 [oc][3][3][c].  When c is a
+ * multiple of 64 and w <= 128 the convolution runs as an implicit GEMM (the
+ * shifted taps are TMA-loaded from `src`, zero outside the map) with the
+ * LayerNorm fused into the tcgen05 GEMM epilogue and the workspace is not
+ * used; otherwise as an im2col into `workspace` followed by that GEMM.  The
+ * workspace must hold rfdetr_b200_op_conv3x3_workspace(batch, h, w, c) bytes
+ * of device memory either way. */
 size_t rfdetr_b200_op_conv3x3_workspace(int batch, int h, int w, int c);
 int rfdetr_b200_op_conv3x3(const void* src, int lds, int batch, int h, int w, int c, const void* weight, int oc,
                            const float* ln_g, const float* ln_b, float eps, int act, float* out32, int ld32,

@@ -397,7 +397,6 @@ rfdetr_status Engine::alloc_activations(int B) {
         {(void**)&taps_, Mp * L_ * D_ * 2},
         {(void**)&cat_, Mp * (2 + bnecks_.size()) * Cb_ * 2},
         {(void**)&tmp128_, Mp * Cb_ * 2},
-        {(void**)&col3_, Mp * 9 * Cb_ * 2},
         {(void**)&p32a_, Mp * Dm_ * 4},
         {(void**)&proj32_, Mp * Dm_ * 4},
         {(void**)&mem16_, Mp * Dm_ * 2},
@@ -503,6 +502,20 @@ struct Launcher {
         if (ln) { a.ln_g = ln->g; a.ln_b = ln->b; a.ln_eps = eps; }
         a.resid = resid; a.ldr = ldr;
         a.out32 = out32; a.ld32 = ld32; a.out16 = out16; a.ld16 = ld16;
+        a.err = err;
+        check(rfb::gemm(a, st), what);
+    }
+    // ConvX: 3x3 convolution (implicit GEMM over the channels-last map `src`,
+    // B images of h x w pixels, c channels at pitch lds) + LayerNorm + SiLU.
+    void conv3(const char* what, const __half* src, int lds, int B, int h, int w, int c, const DLin& W,
+               __half* out16, int ld16, const DNorm* ln, float eps) {
+        GemmArgs a;
+        a.conv_src = src; a.conv_lds = lds; a.conv_h = h; a.conv_w = w; a.conv_c = c;
+        a.B = W.w; a.ldb = W.ldw;
+        a.M = B * h * w; a.N = W.N; a.K = W.K;
+        a.epi = EPI_LN; a.act = ACT_SILU; a.bias = W.b;
+        a.ln_g = ln->g; a.ln_b = ln->b; a.ln_eps = eps;
+        a.out16 = out16; a.ld16 = ld16;
         a.err = err;
         check(rfb::gemm(a, st), what);
     }
@@ -646,13 +659,9 @@ rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int 
     L.gemm("proj.cv1", taps_, L_ * D, Mp, cv1_, EPI_LN, ACT_SILU, nullptr, 0, cat_, Ccat, nullptr, &cv1n_, 1e-6f);
     const __half* cur = cat_ + Cb;
     for (size_t j = 0; j < bnecks_.size(); ++j) {
-        L.check(im2col3x3(cur, Ccat, B, G, G, Cb, col3_, st), "im2col");
-        L.gemm("bneck.cv1", col3_, 9 * Cb, Mp, bnecks_[j].c1, EPI_LN, ACT_SILU, nullptr, 0, tmp128_, Cb, nullptr,
-               &bnecks_[j].n1, 1e-6f);
-        L.check(im2col3x3(tmp128_, Cb, B, G, G, Cb, col3_, st), "im2col");
+        L.conv3("bneck.cv1", cur, Ccat, B, G, G, Cb, bnecks_[j].c1, tmp128_, Cb, &bnecks_[j].n1, 1e-6f);
         __half* dst = cat_ + (2 + j) * Cb;
-        L.gemm("bneck.cv2", col3_, 9 * Cb, Mp, bnecks_[j].c2, EPI_LN, ACT_SILU, nullptr, 0, dst, Ccat, nullptr,
-               &bnecks_[j].n2, 1e-6f);
+        L.conv3("bneck.cv2", tmp128_, Cb, B, G, G, Cb, bnecks_[j].c2, dst, Ccat, &bnecks_[j].n2, 1e-6f);
         cur = dst;
     }
     L.gemm("proj.cv2", cat_, Ccat, Mp, cv2_, EPI_LN, ACT_SILU, p32a_, Dm, nullptr, 0, nullptr, &cv2n_, 1e-6f);

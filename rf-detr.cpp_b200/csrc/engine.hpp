@@ -171,7 +171,6 @@ private:
     __half* taps_ = nullptr;
     __half* cat_ = nullptr;
     __half* tmp128_ = nullptr;
-    __half* col3_ = nullptr;
     float* p32a_ = nullptr;
     float* proj32_ = nullptr;
     __half* mem16_ = nullptr;

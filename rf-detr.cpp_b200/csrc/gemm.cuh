@@ -55,6 +55,15 @@ struct GemmArgs {
     int patch_ntok = 0;    // tokens per image
     const float* posw = nullptr;  // [ntok][N] windowed pos-embed
     int ln_pre32 = 0;      // EPI_LN: out32 receives the sum before normalisation (set for EPI_RESID_LN)
+    // Implicit-GEMM 3x3 convolution (stride 1, zero padding 1): when conv_src is
+    // set, A is not read from memory as a matrix; row (b, y, x), column
+    // (tap, c) of A is conv_src[b][y + tap/3 - 1][x + tap%3 - 1][c] (zero
+    // outside the map), loaded by 4-D TMA boxes straight from the channels-last
+    // map [b][conv_h][conv_w] with pixel pitch conv_lds.  M = b * conv_h *
+    // conv_w, K = 9 * conv_c (conv_c a multiple of 64), B = weights [N][3][3][c].
+    const __half* conv_src = nullptr;
+    int conv_lds = 0, conv_h = 0, conv_w = 0, conv_c = 0;
+    int conv_r = 0;        // set by the launcher: image rows per 128-row tile
     int* err = nullptr;    // device error word
     int tma_out = 0;       // set by the launcher: outputs written through TMA stores
 };

@@ -59,6 +59,19 @@ extern "C" int rfdetr_b200_op_conv3x3(const void* src, int lds, int batch, int h
     if (!src || !weight || !workspace || need == 0 || workspace_bytes < need) return (int)cudaErrorInvalidValue;
     if ((oc != 128 && oc != 256) || (act != rfb::ACT_NONE && act != rfb::ACT_SILU)) return (int)cudaErrorInvalidValue;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (c % 64 == 0 && w <= 128) {
+        // implicit GEMM: the 3x3 taps are TMA-loaded straight from `src` (the workspace is not touched)
+        rfb::GemmArgs a;
+        a.conv_src = static_cast<const __half*>(src);
+        a.conv_lds = lds; a.conv_h = h; a.conv_w = w; a.conv_c = c;
+        a.B = static_cast<const __half*>(weight); a.ldb = 9 * c;
+        a.M = batch * h * w; a.N = oc; a.K = 9 * c;
+        a.epi = rfb::EPI_LN; a.act = act;
+        a.ln_g = ln_g; a.ln_b = ln_b; a.ln_eps = eps;
+        a.out32 = out32; a.ld32 = ld32;
+        a.out16 = static_cast<__half*>(out16); a.ld16 = ld16;
+        return (int)rfb::gemm(a, st);
+    }
     __half* col = static_cast<__half*>(workspace);
     cudaError_t e = rfb::im2col3x3(static_cast<const __half*>(src), lds, batch, h, w, c, col, st);
     if (e != cudaSuccess) return (int)e;

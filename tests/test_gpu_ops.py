@@ -176,12 +176,19 @@ def test_deform_matches_grid_sample():
 
 
 @pytest.mark.parametrize("oc,act", [(128, 3), (256, 0)])
-def test_conv3x3_layernorm(oc, act):
-    """ConvX block (3x3 conv, channel LN, SiLU) against torch conv2d."""
-    torch.manual_seed(oc)
+@pytest.mark.parametrize("B,H,W,Cin,lds", [(2, 9, 7, 128, 128), (3, 40, 40, 128, 640), (2, 24, 24, 64, 64),
+                                           (1, 44, 44, 128, 128), (1, 5, 130, 64, 64), (2, 6, 6, 96, 96)])
+def test_conv3x3_layernorm(oc, act, B, H, W, Cin, lds):
+    """ConvX block (3x3 conv, channel LN, SiLU) against torch conv2d.
+
+    Cin % 64 == 0 and W <= 128 take the implicit GEMM (image rows per 128-row
+    tile: 18, 3 with a partial last tile, 5, 2); W = 130 and Cin = 96 take the
+    im2col path.  lds > Cin reads the input out of a wider channel-concat map.
+    """
+    torch.manual_seed(oc + H)
     dev = "cuda:0"
-    B, H, W, Cin = 2, 9, 7, 128
-    x = torch.randn(B, H, W, Cin, device=dev).half()
+    xw = torch.randn(B, H, W, lds, device=dev).half()
+    x = xw[..., :Cin]
     w = (torch.randn(oc, Cin, 3, 3, device=dev) * 0.05)
     wk = w.permute(0, 2, 3, 1).contiguous().half()  # [oc][ky][kx][c]
     g = torch.rand(oc, device=dev) + 0.5
@@ -196,13 +203,13 @@ def test_conv3x3_layernorm(oc, act):
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     out16 = torch.zeros(B * H * W, oc, dtype=torch.float16, device=dev)
     out32 = torch.zeros(B * H * W, oc, device=dev)
-    rc = L.rfdetr_b200_op_conv3x3(_p(x), Cin, B, H, W, Cin, _p(wk), oc, _p(g), _p(b), 1e-6, act, _p(out32), oc,
+    rc = L.rfdetr_b200_op_conv3x3(_p(xw), lds, B, H, W, Cin, _p(wk), oc, _p(g), _p(b), 1e-6, act, _p(out32), oc,
                                   _p(out16), oc, _p(ws), ws_bytes, _stream())
     assert rc == 0
     torch.cuda.synchronize()
     assert rel(out32, ref.reshape(-1, oc)) < 1e-4
     assert rel(out16, ref.reshape(-1, oc)) < 2e-3
     # a workspace that is too small is rejected before any launch
-    assert L.rfdetr_b200_op_conv3x3(_p(x), Cin, B, H, W, Cin, _p(wk), oc, _p(g), _p(b), 1e-6, act, _p(out32), oc,
+    assert L.rfdetr_b200_op_conv3x3(_p(xw), lds, B, H, W, Cin, _p(wk), oc, _p(g), _p(b), 1e-6, act, _p(out32), oc,
                                     _p(out16), oc, _p(ws), ws_bytes - 1, _stream()) != 0
 
