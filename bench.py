@@ -129,6 +129,7 @@ def backbone_gemm_flops(cfg, batch):
     D, F = cfg["backbone"]["dim"], cfg["backbone"]["ffn_dim"]
     M = batch * ntok
     per = {"qkv": 2 * M * D * 3 * D, "proj": 2 * M * D * D, "fc1": 2 * M * D * F, "fc2": 2 * M * F * D}
+    per["mlp"] = per["fc1"] + per["fc2"]  # the fused fc1 -> GELU -> fc2 launch
     return per
 
 
@@ -310,8 +311,7 @@ def main():
         if name in g_ms:
             g_ms[name] += t_ms
             g_n[name] += 1
-    depth = cfg["backbone"]["depth"]
-    gemm_flops = sum(fl[k] * depth for k in fl)
+    gemm_flops = sum(fl[k] * g_n[k] for k in fl)  # per launch actually made
     gemm_ms = sum(g_ms.values())
     total_ms = sum(t for _, t in prof)
     hbm, tf_burst, tf_sus, src = peaks()
@@ -365,7 +365,8 @@ def main():
                     "d2h_bytes_per_step": d2h},
             "p50_batch1_ms": round(p50, 3) if p50 is not None else None,
             "gpu_launches": launches,
-            "roofline": {"kernel": "k_gemm (backbone qkv/proj/fc1/fc2 launches)", "bound": "tensor",
+            "roofline": {"kernel": "backbone linears: k_gemm qkv / proj and k_mlp (fc1 -> GELU -> fc2) launches",
+                         "bound": "tensor",
                          "achieved": round(achieved, 1) if achieved else None,
                          "peak": tf_sus, "unit": "TFLOP/s",
                          "frac": round(achieved / tf_sus, 4) if achieved else None,

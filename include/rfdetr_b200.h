@@ -120,6 +120,17 @@ int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ldb, int M, i
 int rfdetr_b200_op_attention(const void* q, const void* k, const void* v, int ldq, int ldk, int ldv, void* o,
                              int ldo, int seq_len, int groups, int heads, int head_dim, float scale, void* stream);
 
+/* Fused transformer MLP, the residual update of a DINOv2 block
+ * (src/dinov2.cpp:93-101 with the layer scale and residual of :483-486):
+ *   x[m] += ls * (GELU(h[m] . W1^T + b1) . W2^T + b2)
+ * h f16 [M][D] (pitch ldh), W1 f16 [F][D] (pitch ldw1), b1 f32 [F], W2 f16
+ * [D][F] (pitch ldw2), b2 f32 [D], ls f32 [D] or NULL (= 1), x f32 [M][D]
+ * (pitch ldx) updated in place.  GELU is the erf form; its output is rounded to
+ * f16 as the operand of the second product; the F-wide hidden activations stay
+ * on chip.  Requires D a multiple of 128 up to 384 and F a multiple of 128. */
+int rfdetr_b200_op_mlp(const void* h, int ldh, const void* w1, int ldw1, const float* b1, const void* w2, int ldw2,
+                       const float* b2, const float* ls, float* x, int ldx, int M, int D, int F, void* stream);
+
 /* Deformable sampling of one level (value f16 [B*G*G][Dm], so_aw f32
  * [B*NQ][ld] = offsets (heads*points*2) then attention logits
  * (heads*points), refpoints f32 [B*NQ][4]) -> out f16 [B*NQ][Dm]. */

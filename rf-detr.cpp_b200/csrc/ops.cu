@@ -3,6 +3,7 @@
 
 #include "gemm.cuh"
 #include "kernels.cuh"
+#include "mlp.cuh"
 
 extern "C" int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int epi,
                                    int act, const float* bias, const float* colscale, const float* ln_g,
@@ -38,6 +39,19 @@ extern "C" int rfdetr_b200_op_attention(const void* q, const void* k, const void
     return (int)rfb::attention(static_cast<const __half*>(q), static_cast<const __half*>(k),
                                static_cast<const __half*>(v), ldq, ldk, ldv, static_cast<__half*>(o), ldo, seq_len,
                                groups, heads, head_dim, scale, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int rfdetr_b200_op_mlp(const void* h, int ldh, const void* w1, int ldw1, const float* b1, const void* w2,
+                                  int ldw2, const float* b2, const float* ls, float* x, int ldx, int M, int D, int F,
+                                  void* stream) {
+    if (!h || !w1 || !w2 || !b1 || !b2 || !x || M < 0 || !rfb::mlp_supported(D, F)) return (int)cudaErrorInvalidValue;
+    rfb::MlpArgs a;
+    a.h = static_cast<const __half*>(h); a.ldh = ldh;
+    a.w1 = static_cast<const __half*>(w1); a.ldw1 = ldw1; a.b1 = b1;
+    a.w2 = static_cast<const __half*>(w2); a.ldw2 = ldw2; a.b2 = b2;
+    a.ls = ls; a.x = x; a.ldx = ldx;
+    a.M = M; a.D = D; a.F = F;
+    return (int)rfb::mlp_fused(a, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int rfdetr_b200_op_deform(const void* value, const float* so_aw, int ld_soaw, const float* refp, int batch,

@@ -113,6 +113,9 @@ SIGNATURES = {
     "rfdetr_b200_op_attention": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                            C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                            C.c_void_p]),
+    "rfdetr_b200_op_mlp": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_void_p]),
     "rfdetr_b200_op_deform": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                         C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "rfdetr_b200_op_conv3x3_workspace": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
