@@ -55,6 +55,15 @@ rfdetr_status rfdetr_b200_sync(rfdetr_context* ctx);
 rfdetr_status rfdetr_b200_device_outputs(rfdetr_context* ctx, const float** d_logits, const float** d_boxes,
                                          const float** d_masks);
 
+/* One selected detection as the device post-process writes it (32 bytes). */
+typedef struct rfdetr_b200_det {
+    int32_t query;     /* decoder query it came from */
+    int32_t class_id;
+    float   score;     /* sigmoid of the winning class logit */
+    float   x1, y1, x2, y2;  /* pixel box in the original image, clamped to it */
+    float   pad;
+} rfdetr_b200_det;
+
 /* Batched rfdetr_detect: n images (any sizes) -> per-image detection arrays.
  * out_dets[i] / out_counts[i] follow rfdetr_detect's ownership rules
  * (free each with rfdetr_detections_free). */
@@ -119,6 +128,30 @@ int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ldb, int M, i
  * [h*head_dim, (h+1)*head_dim) of each operand. */
 int rfdetr_b200_op_attention(const void* q, const void* k, const void* v, int ldq, int ldk, int ldv, void* o,
                              int ldo, int seq_len, int groups, int heads, int head_dim, float scale, void* stream);
+
+/* Post-processing on the device (src/postprocess.cpp:43-181): for each image
+ * b of a batch, the sigmoid-argmax over the nc classes of each of the nq
+ * queries (d_logits f32 [batch][nq][nc], d_boxes f32 [batch][nq][4] cxcywh in
+ * [0,1]), score > threshold, class filter (d_class_filter: filter_len class
+ * ids, or NULL), descending score (ties: lower query first), at most top_k
+ * (0 = all), boxes to clamped pixel xyxy of an img_w x img_h image.  Writes
+ * d_out[b][0 .. d_counts[b]).  nq <= 1024.  All pointers are device memory. */
+int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes, int batch, int nq, int nc, float threshold,
+                          int top_k, const uint32_t* d_class_filter, int filter_len, int img_w, int img_h,
+                          rfdetr_b200_det* d_out, int* d_counts, void* stream);
+
+/* 32-bit words of one bit-packed img_w x img_h mask (rows padded to 32 pixels). */
+size_t rfdetr_b200_mask_bits_words(int img_w, int img_h);
+
+/* Segmentation masks of the selected detections (d_dets / d_counts from
+ * rfdetr_b200_op_select): the query's side x side mask logits (d_masks f32
+ * [batch][nq][side][side]) upsampled bilinearly (half-pixel centres, clamped
+ * edges) to img_w x img_h and thresholded at sigmoid > 0.5; bit j of word
+ * (y, w) of d_bits[b][i] is pixel (32 w + j, y).  d_bits holds batch x
+ * max_dets masks of rfdetr_b200_mask_bits_words words; detections i >=
+ * d_counts[b] are left untouched. */
+int rfdetr_b200_op_mask_bits(const float* d_masks, int batch, int nq, int side, const rfdetr_b200_det* d_dets,
+                             const int* d_counts, int max_dets, int img_w, int img_h, uint32_t* d_bits, void* stream);
 
 /* Fused transformer MLP, the residual update of a DINOv2 block
  * (src/dinov2.cpp:93-101 with the layer scale and residual of :483-486):

@@ -840,6 +840,7 @@ inline float sigmoid_stable(float x) {
 
 extern "C" int oracle_select(const float* logits, const float* boxes, int nq, int nc,
                              float threshold, int top_k, int img_w, int img_h,
+                             const uint32_t* class_filter, int filter_len,
                              int32_t* out_query, int32_t* out_class, float* out_score, float* out_xyxy) {
     struct Cand { int q, c; float s; };
     std::vector<Cand> cands;
@@ -850,6 +851,12 @@ extern "C" int oracle_select(const float* logits, const float* boxes, int nq, in
             if (s > bs) { bs = s; bc = ci; }
         }
         if (bs <= threshold) continue;
+        // class filter (src/postprocess.cpp:43-113): keep only listed classes
+        if (class_filter && filter_len > 0) {
+            bool allowed = false;
+            for (int i = 0; i < filter_len; ++i) allowed |= class_filter[i] == (uint32_t)bc;
+            if (!allowed) continue;
+        }
         cands.push_back({q, bc, bs});
     }
     std::stable_sort(cands.begin(), cands.end(), [](const Cand& a, const Cand& b) { return a.s > b.s; });

@@ -79,6 +79,7 @@ void oracle_bicubic_resample(const float* src, int src_side, int dim, float* dst
  * fills out_query/out_class/out_score/out_xyxy (capacity num_queries). */
 int oracle_select(const float* logits, const float* boxes, int nq, int nc,
                   float threshold, int top_k, int img_w, int img_h,
+                  const uint32_t* class_filter, int filter_len,
                   int32_t* out_query, int32_t* out_class, float* out_score, float* out_xyxy);
 
 /* src/postprocess.cpp:132-181: bilinear upsample + sigmoid threshold. */

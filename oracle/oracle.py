@@ -61,7 +61,7 @@ def lib():
                                               C.POINTER(C.c_float), C.c_int]
         L.oracle_select.restype = C.c_int
         L.oracle_select.argtypes = [C.POINTER(C.c_float), C.POINTER(C.c_float), C.c_int, C.c_int,
-                                    C.c_float, C.c_int, C.c_int, C.c_int,
+                                    C.c_float, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_uint32), C.c_int,
                                     C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.POINTER(C.c_float),
                                     C.POINTER(C.c_float)]
         L.oracle_mask_upsample.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int, C.c_int,
@@ -163,7 +163,7 @@ class Oracle:
         return {"logits": logits, "boxes": boxes, "topk": topk, "masks": masks, "trace": store}
 
 
-def select(logits, boxes, threshold, top_k, img_w, img_h):
+def select(logits, boxes, threshold, top_k, img_w, img_h, class_filter=None):
     nq, nc = logits.shape
     q = np.zeros(nq, np.int32)
     c = np.zeros(nq, np.int32)
@@ -171,7 +171,10 @@ def select(logits, boxes, threshold, top_k, img_w, img_h):
     xy = np.zeros((nq, 4), np.float32)
     lg = np.ascontiguousarray(logits, np.float32)
     bx = np.ascontiguousarray(boxes, np.float32)
+    flt = None if class_filter is None else np.ascontiguousarray(class_filter, np.uint32)
     n = lib().oracle_select(_fp(lg), _fp(bx), nq, nc, threshold, top_k, img_w, img_h,
+                            None if flt is None else flt.ctypes.data_as(C.POINTER(C.c_uint32)),
+                            0 if flt is None else len(flt),
                             q.ctypes.data_as(C.POINTER(C.c_int32)), c.ctypes.data_as(C.POINTER(C.c_int32)),
                             _fp(s), _fp(xy))
     return q[:n], c[:n], s[:n], xy[:n]

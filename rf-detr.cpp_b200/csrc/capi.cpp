@@ -12,6 +12,7 @@
 #include "image_io.hpp"
 #include "model.hpp"
 #include "postprocess.hpp"
+#include "select.cuh"
 
 #include <cstdlib>
 #include <cstring>
@@ -32,10 +33,50 @@ struct rfdetr_context {
     size_t h_in_cap = 0;
     float* h_out = nullptr;
     size_t h_out_cap = 0;
+    // device post-process: records, counts, class filter and bit masks on the
+    // device; pinned host copies of what comes back
+    rfdetr_b200_det* d_dets = nullptr;
+    int* d_counts = nullptr;
+    uint32_t* d_filter = nullptr;
+    uint32_t* d_bits = nullptr;
+    size_t dets_cap = 0, counts_cap = 0, filter_cap = 0, bits_cap = 0;
+    rfdetr_b200_det* h_dets = nullptr;
+    int* h_counts = nullptr;
+    uint32_t* h_bits = nullptr;
+    size_t h_dets_cap = 0, h_counts_cap = 0, h_bits_cap = 0;
 
     ~rfdetr_context() {
         if (h_in) cudaFreeHost(h_in);
         if (h_out) cudaFreeHost(h_out);
+        if (h_dets) cudaFreeHost(h_dets);
+        if (h_counts) cudaFreeHost(h_counts);
+        if (h_bits) cudaFreeHost(h_bits);
+        if (engine) cudaSetDevice(engine->device());
+        if (d_dets) cudaFree(d_dets);
+        if (d_counts) cudaFree(d_counts);
+        if (d_filter) cudaFree(d_filter);
+        if (d_bits) cudaFree(d_bits);
+    }
+    // grow-only buffers (elements of T); false on allocation failure
+    template <typename T>
+    static bool grow_dev(T** p, size_t* cap, size_t n) {
+        if (n <= *cap) return true;
+        if (*p) cudaFree(*p);
+        *p = nullptr;
+        *cap = 0;
+        if (cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T)) != cudaSuccess) return false;
+        *cap = n;
+        return true;
+    }
+    template <typename T>
+    static bool grow_host(T** p, size_t* cap, size_t n) {
+        if (n <= *cap) return true;
+        if (*p) cudaFreeHost(*p);
+        *p = nullptr;
+        *cap = 0;
+        if (cudaMallocHost(reinterpret_cast<void**>(p), n * sizeof(T)) != cudaSuccess) return false;
+        *cap = n;
+        return true;
     }
     bool stage_in(size_t bytes) {
         if (bytes <= h_in_cap) return true;
@@ -131,6 +172,93 @@ void attach_names(const rfdetr_context* ctx, rfdetr_detection* d, size_t n) {
         if (d[i].class_id < names.size()) d[i].class_name = names[d[i].class_id].c_str();
 }
 
+// Post-process the last forward of `batch` images of w x h pixels on the
+// device (select.cu) and build the per-image rfdetr_detection arrays: only the
+// selected records and their bit masks cross PCIe; the 0/255 masks of the
+// reference API are expanded from the bits on the host.
+rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, const rfdetr_detect_params* params,
+                                 rfdetr_detection** out_dets, size_t* out_counts) {
+    rfb::Engine& e = *ctx->engine;
+    const rfb::Config& c = ctx->model->cfg;
+    const int nq = (int)c.num_queries, nc = (int)c.num_classes;
+    const bool seg = c.has_seg && e.masks() != nullptr;
+    const int ms = e.mask_side();
+    const int max_dets = params->top_k > 0 && (int)params->top_k < nq ? (int)params->top_k : nq;
+    const size_t words = rfb::mask_bits_words(w, h);
+    const size_t flen = params->class_filter ? params->class_filter_len : 0;
+    if (RFB_CUDA_FAIL(cudaSetDevice(e.device()))) return RFDETR_ERR_INFERENCE;
+    if (!rfdetr_context::grow_dev(&ctx->d_dets, &ctx->dets_cap, (size_t)batch * nq) ||
+        !rfdetr_context::grow_dev(&ctx->d_counts, &ctx->counts_cap, (size_t)batch) ||
+        (flen && !rfdetr_context::grow_dev(&ctx->d_filter, &ctx->filter_cap, flen)) ||
+        (seg && !rfdetr_context::grow_dev(&ctx->d_bits, &ctx->bits_cap, (size_t)batch * max_dets * words)) ||
+        !rfdetr_context::grow_host(&ctx->h_dets, &ctx->h_dets_cap, (size_t)batch * nq) ||
+        !rfdetr_context::grow_host(&ctx->h_counts, &ctx->h_counts_cap, (size_t)batch))
+        return RFDETR_ERR_OUT_OF_MEMORY;
+    const cudaStream_t st = e.stream();
+    if (flen && RFB_CUDA_FAIL(cudaMemcpyAsync(ctx->d_filter, params->class_filter, flen * 4, cudaMemcpyHostToDevice, st)))
+        return RFDETR_ERR_INFERENCE;
+    if (RFB_CUDA_FAIL(rfb::select_detections_device(e.logits(), e.boxes(), batch, nq, nc, params->threshold,
+                                                    (int)params->top_k, flen ? ctx->d_filter : nullptr, (int)flen, w,
+                                                    h, ctx->d_dets, ctx->d_counts, st)))
+        return RFDETR_ERR_INFERENCE;
+    if (seg && RFB_CUDA_FAIL(rfb::mask_bits_device(e.masks(), batch, nq, ms, ctx->d_dets, ctx->d_counts, max_dets, w,
+                                                   h, ctx->d_bits, st)))
+        return RFDETR_ERR_INFERENCE;
+    if (RFB_CUDA_FAIL(cudaMemcpyAsync(ctx->h_counts, ctx->d_counts, (size_t)batch * sizeof(int), cudaMemcpyDeviceToHost,
+                                      st)) ||
+        RFB_CUDA_FAIL(cudaMemcpyAsync(ctx->h_dets, ctx->d_dets, (size_t)batch * nq * sizeof(rfdetr_b200_det),
+                                      cudaMemcpyDeviceToHost, st)) ||
+        RFB_CUDA_FAIL(cudaStreamSynchronize(st)))
+        return RFDETR_ERR_INFERENCE;
+    size_t kept = 0;
+    for (int b = 0; b < batch; ++b) kept += (size_t)ctx->h_counts[b];
+    if (seg && kept) {
+        if (!rfdetr_context::grow_host(&ctx->h_bits, &ctx->h_bits_cap, kept * words)) return RFDETR_ERR_OUT_OF_MEMORY;
+        size_t off = 0;
+        for (int b = 0; b < batch; ++b) {
+            const size_t n = (size_t)ctx->h_counts[b] * words;
+            if (n && RFB_CUDA_FAIL(cudaMemcpyAsync(ctx->h_bits + off, ctx->d_bits + (size_t)b * max_dets * words,
+                                                   n * 4, cudaMemcpyDeviceToHost, st)))
+                return RFDETR_ERR_INFERENCE;
+            off += n;
+        }
+        if (RFB_CUDA_FAIL(cudaStreamSynchronize(st))) return RFDETR_ERR_INFERENCE;
+    }
+    size_t off = 0;
+    for (int b = 0; b < batch; ++b) {
+        const int n = ctx->h_counts[b];
+        out_dets[b] = nullptr;
+        out_counts[b] = 0;
+        if (n <= 0) continue;
+        auto* d = static_cast<rfdetr_detection*>(std::calloc((size_t)n, sizeof(rfdetr_detection)));
+        if (!d) return RFDETR_ERR_OUT_OF_MEMORY;
+        for (int i = 0; i < n; ++i) {
+            const rfdetr_b200_det& r = ctx->h_dets[(size_t)b * nq + i];
+            d[i].class_id = (uint32_t)r.class_id;
+            d[i].score = r.score;
+            d[i].x1 = r.x1; d[i].y1 = r.y1; d[i].x2 = r.x2; d[i].y2 = r.y2;
+            if (seg) {
+                auto* m = static_cast<uint8_t*>(std::malloc((size_t)w * h));
+                if (m) {
+                    const uint32_t* src = ctx->h_bits + off + (size_t)i * words;
+                    const size_t wpr = (size_t)(w + 31) / 32;
+                    for (int y = 0; y < h; ++y)
+                        for (int x = 0; x < w; ++x)
+                            m[(size_t)y * w + x] = (src[y * wpr + (x >> 5)] >> (x & 31)) & 1u ? 255 : 0;
+                }
+                d[i].mask = m;
+                d[i].mask_width = m ? w : 0;
+                d[i].mask_height = m ? h : 0;
+            }
+        }
+        off += (size_t)n * words;
+        attach_names(ctx, d, (size_t)n);
+        out_dets[b] = d;
+        out_counts[b] = (size_t)n;
+    }
+    return RFDETR_OK;
+}
+
 }  // namespace
 
 // ============================================================================
@@ -167,19 +295,11 @@ extern "C" rfdetr_status rfdetr_detect(rfdetr_context* ctx, const rfdetr_image* 
         rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_detect: model forward failed");
         return RFDETR_ERR_INFERENCE;
     }
-    const rfb::Config& c = ctx->model->cfg;
-    const size_t nq = c.num_queries, nc = c.num_classes;
-    const int ms = ctx->engine->mask_side();
-    const size_t need = nq * nc + nq * 4 + (c.has_seg ? nq * (size_t)ms * ms : 0);
-    if (!ctx->stage_out(need)) return RFDETR_ERR_OUT_OF_MEMORY;
-    float* lg = ctx->h_out;
-    float* bx = lg + nq * nc;
-    float* mk = c.has_seg ? bx + nq * 4 : nullptr;
-    s = fetch_outputs(ctx, 1, lg, bx, mk);
-    if (s != RFDETR_OK) return RFDETR_ERR_INFERENCE;
-    rfb::select_detections(lg, bx, mk, ms, ms, nq, nc, params->threshold, params->top_k, params->class_filter,
-                           params->class_filter_len, img->width, img->height, out_detections, out_n);
-    if (*out_detections) attach_names(ctx, *out_detections, *out_n);
+    s = postprocess_device(ctx, 1, img->width, img->height, params, out_detections, out_n);
+    if (s != RFDETR_OK) {
+        rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_detect: post-processing failed");
+        return s == RFDETR_ERR_OUT_OF_MEMORY ? s : RFDETR_ERR_INFERENCE;
+    }
     return RFDETR_OK;
 }
 
@@ -247,10 +367,6 @@ extern "C" rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfd
     if (n == 0) return RFDETR_OK;
     // Same-sized runs go through one batched forward; the preprocess kernel
     // resizes each run to the model resolution on the GPU.
-    const rfb::Config& c = ctx->model->cfg;
-    const size_t nq = c.num_queries, nc = c.num_classes;
-    const int ms = ctx->engine->mask_side();
-    const size_t per = nq * nc + nq * 4 + (c.has_seg ? nq * (size_t)ms * ms : 0);
     size_t i = 0;
     while (i < n) {
         if (!imgs[i] || imgs[i]->rgb.empty()) return RFDETR_ERR_INVALID_ARG;
@@ -263,19 +379,8 @@ extern "C" rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfd
         for (size_t k = i; k < j; ++k) std::memcpy(ctx->h_in + (k - i) * img_bytes, imgs[k]->rgb.data(), img_bytes);
         rfdetr_status s = forward_rgb_impl(ctx, ctx->h_in, batch, w, h);
         if (s != RFDETR_OK) return RFDETR_ERR_INFERENCE;
-        if (!ctx->stage_out(per * batch)) return RFDETR_ERR_OUT_OF_MEMORY;
-        float* lg = ctx->h_out;
-        float* bx = lg + (size_t)batch * nq * nc;
-        float* mk = c.has_seg ? bx + (size_t)batch * nq * 4 : nullptr;
-        s = fetch_outputs(ctx, batch, lg, bx, mk);
+        s = postprocess_device(ctx, batch, w, h, params, out_dets + i, out_counts + i);
         if (s != RFDETR_OK) return s;
-        for (int k = 0; k < batch; ++k) {
-            rfb::select_detections(lg + (size_t)k * nq * nc, bx + (size_t)k * nq * 4,
-                                   mk ? mk + (size_t)k * nq * ms * ms : nullptr, ms, ms, nq, nc, params->threshold,
-                                   params->top_k, params->class_filter, params->class_filter_len, w, h,
-                                   &out_dets[i + k], &out_counts[i + k]);
-            if (out_dets[i + k]) attach_names(ctx, out_dets[i + k], out_counts[i + k]);
-        }
         i = j;
     }
     return RFDETR_OK;

@@ -4,6 +4,7 @@
 #include "gemm.cuh"
 #include "kernels.cuh"
 #include "mlp.cuh"
+#include "select.cuh"
 
 extern "C" int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int epi,
                                    int act, const float* bias, const float* colscale, const float* ln_g,
@@ -39,6 +40,25 @@ extern "C" int rfdetr_b200_op_attention(const void* q, const void* k, const void
     return (int)rfb::attention(static_cast<const __half*>(q), static_cast<const __half*>(k),
                                static_cast<const __half*>(v), ldq, ldk, ldv, static_cast<__half*>(o), ldo, seq_len,
                                groups, heads, head_dim, scale, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes, int batch, int nq, int nc,
+                                     float threshold, int top_k, const uint32_t* d_class_filter, int filter_len,
+                                     int img_w, int img_h, rfdetr_b200_det* d_out, int* d_counts, void* stream) {
+    return (int)rfb::select_detections_device(d_logits, d_boxes, batch, nq, nc, threshold, top_k, d_class_filter,
+                                              filter_len, img_w, img_h, d_out, d_counts,
+                                              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t rfdetr_b200_mask_bits_words(int img_w, int img_h) {
+    return (img_w > 0 && img_h > 0) ? rfb::mask_bits_words(img_w, img_h) : 0;
+}
+
+extern "C" int rfdetr_b200_op_mask_bits(const float* d_masks, int batch, int nq, int side,
+                                        const rfdetr_b200_det* d_dets, const int* d_counts, int max_dets, int img_w,
+                                        int img_h, uint32_t* d_bits, void* stream) {
+    return (int)rfb::mask_bits_device(d_masks, batch, nq, side, d_dets, d_counts, max_dets, img_w, img_h, d_bits,
+                                      static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int rfdetr_b200_op_mlp(const void* h, int ldh, const void* w1, int ldw1, const float* b1, const void* w2,

@@ -38,6 +38,12 @@ class Detection(C.Structure):
                 ("mask", C.POINTER(C.c_uint8)), ("mask_width", C.c_int), ("mask_height", C.c_int)]
 
 
+class B200Det(C.Structure):
+    """rfdetr_b200_det: one selected detection written by rfdetr_b200_op_select (32 bytes)."""
+    _fields_ = [("query", C.c_int32), ("class_id", C.c_int32), ("score", C.c_float), ("x1", C.c_float),
+                ("y1", C.c_float), ("x2", C.c_float), ("y2", C.c_float), ("pad", C.c_float)]
+
+
 class B200Params(C.Structure):
     _fields_ = [("device", C.c_int), ("max_batch", C.c_int)]
 
@@ -113,6 +119,11 @@ SIGNATURES = {
     "rfdetr_b200_op_attention": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                            C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                            C.c_void_p]),
+    "rfdetr_b200_op_select": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
+                                        C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "rfdetr_b200_mask_bits_words": (C.c_size_t, [C.c_int, C.c_int]),
+    "rfdetr_b200_op_mask_bits": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                           C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "rfdetr_b200_op_mlp": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                      C.c_void_p]),

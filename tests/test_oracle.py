@@ -107,6 +107,12 @@ def test_select_and_mask_upsample():
     assert np.array_equal(q, order)
     assert np.allclose(s, best[order], rtol=1e-6)
     assert np.all(xy[:, 0] >= 0) and np.all(xy[:, 2] <= 640)
+    # class filter (applied before the sort and top_k)
+    qf, cf, sf, _ = O.select(logits, boxes, 0.5, 7, 640, 480, class_filter=[1, 3])
+    cls = sig.argmax(1)
+    keepf = np.where((best > 0.5) & np.isin(cls, [1, 3]))[0]
+    orderf = keepf[np.argsort(-best[keepf], kind="stable")][:7]
+    assert np.array_equal(qf, orderf) and set(cf.tolist()) <= {1, 3}
     m = rng.standard_normal((6, 6)).astype(np.float32)
     up = O.mask_upsample(m, 18, 12)
     t = torch.from_numpy(m)[None, None].double()
