@@ -19,8 +19,12 @@ extern "C" {
 #endif
 
 typedef struct {
-    int device;     /* CUDA device ordinal (default 0) */
-    int max_batch;  /* images the activation arena is sized for at init (grows on demand) */
+    int device;       /* CUDA device ordinal (default 0) */
+    int max_batch;    /* images the activation arena is sized for at init (grows on demand) */
+    int weight_type;  /* 0: weights as stored; else re-quantize at load, on the GPU, every
+                         quantizable weight stored as F32/F16/BF16 to this GGUF type (1 F16,
+                         8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K; K-quants fall back to Q8_0 for
+                         rows that are not a multiple of 256), as rfdetr_b200_quantize_gguf */
 } rfdetr_b200_params;
 
 /* Replaces rfdetr_init (src/rfdetr.cpp:37-107) with an explicit device and
@@ -128,6 +132,20 @@ int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ldb, int M, i
  * [h*head_dim, (h+1)*head_dim) of each operand. */
 int rfdetr_b200_op_attention(const void* q, const void* k, const void* v, int ldq, int ldk, int ldv, void* o,
                              int ldo, int seq_len, int groups, int heads, int head_dim, float scale, void* stream);
+
+/* The reference's `rfdetr-cli quantize` (examples/cli/main.cpp:387-640):
+ * write a copy of the GGUF at in_path to out_path with every quantizable
+ * weight (2-D `.weight` tensors with both dims >= 64 and rows a multiple of
+ * 32, embeddings excluded) that is stored as F32 / F16 / BF16 re-quantized to
+ * `type` (1 F16, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K; K-quants fall back to
+ * Q8_0 for rows that are not a multiple of 256).  The block quantizers run on
+ * CUDA device `device`; metadata and every other tensor are copied unchanged. */
+rfdetr_status rfdetr_b200_quantize_gguf(const char* in_path, const char* out_path, int type, int device);
+
+/* The block quantizers behind rfdetr_b200_quantize_gguf: n f32 values
+ * (device memory, n a multiple of the block size: 1 F16, 32 Q8_0, 256 Q4_K /
+ * Q5_K / Q6_K) -> GGUF blocks of `type` at d_out (device memory). */
+int rfdetr_b200_op_quantize(int type, const float* d_src, long long n, void* d_out, void* stream);
 
 /* Post-processing on the device (src/postprocess.cpp:43-181): for each image
  * b of a batch, the sigmoid-argmax over the nc classes of each of the nq

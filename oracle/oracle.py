@@ -19,7 +19,10 @@ REPO = os.path.dirname(HERE)
 sys.path.insert(0, os.path.join(REPO, "rf-detr.cpp_b200"))
 from rfdetr_b200 import synth  # noqa: E402
 
-TYPE_CODES = {"F32": 0, "F16": 1, "Q8_0": 2, "Q4_K": 3}
+# Weight storage type -> the oracle's activation-rounding class (mode 1): ggml's
+# CPU dot products round activations to f16 for F16 weights, to Q8_0 blocks for
+# Q8_0 weights and to Q8_K blocks for every K-quant (Q4_K, Q5_K, Q6_K).
+TYPE_CODES = {"F32": 0, "F16": 1, "Q8_0": 2, "Q4_K": 3, "Q5_K": 3, "Q6_K": 3}
 
 
 class OracleConfig(C.Structure):

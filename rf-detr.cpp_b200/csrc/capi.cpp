@@ -12,6 +12,7 @@
 #include "image_io.hpp"
 #include "model.hpp"
 #include "postprocess.hpp"
+#include "requant.hpp"
 #include "select.cuh"
 
 #include <cstdlib>
@@ -106,7 +107,8 @@ int resolve_threads(int n) {
     return hc ? (int)hc : 1;
 }
 
-rfdetr_context* init_impl(const rfdetr_params* params, int device, int max_batch, rfdetr_status* out_status) {
+rfdetr_context* init_impl(const rfdetr_params* params, int device, int max_batch, rfdetr_status* out_status,
+                          int weight_type = 0) {
     auto set = [&](rfdetr_status s) { if (out_status) *out_status = s; };
     if (!params || !params->model_path) { set(RFDETR_ERR_INVALID_ARG); return nullptr; }
     if (params->log_cb) rfdetr_set_log_callback(params->log_cb, params->log_user_data);
@@ -115,6 +117,15 @@ rfdetr_context* init_impl(const rfdetr_params* params, int device, int max_batch
     if (!m) { set(st); return nullptr; }
     st = rfb::model_validate(*m);
     if (st != RFDETR_OK) { set(st); return nullptr; }
+    if (weight_type != 0) {
+        std::string err;
+        const int rc = rfb::requantize_model(&m->file, (uint32_t)weight_type, device, &err);
+        if (rc != 0) {
+            rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_init: re-quantization failed: %s", err.c_str());
+            set((rfdetr_status)rc);
+            return nullptr;
+        }
+    }
     auto eng = rfb::Engine::create(*m, device, max_batch, &st);
     if (!eng) { set(st); return nullptr; }
     auto* ctx = new (std::nothrow) rfdetr_context();
@@ -309,7 +320,8 @@ extern "C" rfdetr_status rfdetr_detect(rfdetr_context* ctx, const rfdetr_image* 
 
 extern "C" rfdetr_context* rfdetr_b200_init(const rfdetr_params* params, const rfdetr_b200_params* b,
                                             rfdetr_status* out_status) {
-    return init_impl(params, b ? b->device : 0, b && b->max_batch > 0 ? b->max_batch : 1, out_status);
+    return init_impl(params, b ? b->device : 0, b && b->max_batch > 0 ? b->max_batch : 1, out_status,
+                     b ? b->weight_type : 0);
 }
 
 extern "C" rfdetr_status rfdetr_b200_forward_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width,

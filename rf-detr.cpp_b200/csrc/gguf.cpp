@@ -125,6 +125,8 @@ int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
     const uint64_t n_tensors = r.get<uint64_t>();
     const uint64_t n_kv = r.get<uint64_t>();
     if (!r.ok || n_tensors > 100000 || n_kv > 100000) return fail(-6, "corrupt GGUF header");
+    out->n_kv = n_kv;
+    const long kv_begin = std::ftell(r.f);
     for (uint64_t i = 0; i < n_kv; ++i) {
         std::string key = r.str();
         GgufValue v;
@@ -157,6 +159,16 @@ int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
         if (!r.ok) return fail(-6, "truncated GGUF metadata");
         out->kv.emplace(std::move(key), std::move(v));
     }
+    {
+        // keep the metadata section verbatim (it is copied when the file is rewritten)
+        const long kv_end = std::ftell(r.f);
+        if (kv_begin < 0 || kv_end < kv_begin) return fail(-3, "ftell failed");
+        out->kv_raw.resize((size_t)(kv_end - kv_begin));
+        if (std::fseek(r.f, kv_begin, SEEK_SET) != 0 ||
+            (!out->kv_raw.empty() && std::fread(out->kv_raw.data(), 1, out->kv_raw.size(), r.f) != out->kv_raw.size()) ||
+            std::fseek(r.f, kv_end, SEEK_SET) != 0)
+            return fail(-3, "read failed");
+    }
     out->tensors.resize(n_tensors);
     for (uint64_t i = 0; i < n_tensors; ++i) {
         GgufTensor& t = out->tensors[i];
@@ -177,6 +189,7 @@ int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
     uint64_t align = 32;
     auto ita = out->kv.find("general.alignment");
     if (ita != out->kv.end()) align = ita->second.u ? ita->second.u : 32;
+    out->alignment = align;
     long pos = std::ftell(r.f);
     if (pos < 0) return fail(-3, "ftell failed");
     const uint64_t data_start = ((uint64_t)pos + align - 1) / align * align;
@@ -189,6 +202,60 @@ int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
     out->data.resize(data_size);
     if (std::fseek(r.f, (long)data_start, SEEK_SET) != 0) return fail(-3, "seek failed");
     if (data_size && std::fread(out->data.data(), 1, data_size, r.f) != data_size) return fail(-3, "read failed");
+    return 0;
+}
+
+int gguf_write(const std::string& path, const GgufFile& f, std::string* err) {
+    std::unique_ptr<FILE, int (*)(FILE*)> fp(std::fopen(path.c_str(), "wb"), &std::fclose);
+    if (!fp) {
+        if (err) *err = "cannot open " + path + " for writing";
+        return -3;
+    }
+    FILE* o = fp.get();
+    bool ok = true;
+    auto put = [&](const void* p, size_t n) { ok = ok && (n == 0 || std::fwrite(p, 1, n, o) == n); };
+    auto put64 = [&](uint64_t v) { put(&v, 8); };
+    auto put32 = [&](uint32_t v) { put(&v, 4); };
+    const uint64_t al = f.alignment ? f.alignment : 32;
+    put("GGUF", 4);
+    put32(f.version);
+    put64(f.tensors.size());
+    put64(f.n_kv);
+    put(f.kv_raw.data(), f.kv_raw.size());
+    std::vector<uint64_t> offs(f.tensors.size());
+    uint64_t off = 0;
+    for (size_t i = 0; i < f.tensors.size(); ++i) {
+        const GgufTensor& t = f.tensors[i];
+        offs[i] = off;
+        put64(t.name.size());
+        put(t.name.data(), t.name.size());
+        put32((uint32_t)t.n_dims);
+        for (int d = 0; d < t.n_dims; ++d) put64((uint64_t)t.ne[d]);
+        put32(t.type);
+        put64(off);
+        off += (t.nbytes + al - 1) / al * al;
+    }
+    static const uint8_t zeros[256] = {};
+    auto pad_to = [&](uint64_t pos) {
+        const uint64_t p = (pos + al - 1) / al * al - pos;
+        for (uint64_t k = 0; k < p; k += sizeof(zeros)) put(zeros, std::min<uint64_t>(sizeof(zeros), p - k));
+    };
+    const long hdr = std::ftell(o);
+    if (hdr < 0) ok = false;
+    pad_to((uint64_t)hdr);
+    for (size_t i = 0; i < f.tensors.size() && ok; ++i) {
+        const GgufTensor& t = f.tensors[i];
+        if (t.offset + t.nbytes > f.data.size()) {
+            if (err) *err = "tensor " + t.name + " has no data";
+            return -3;
+        }
+        put(f.data.data() + t.offset, t.nbytes);
+        pad_to(t.nbytes);
+    }
+    if (!ok) {
+        if (err) *err = "write failed: " + path;
+        return -3;
+    }
     return 0;
 }
 

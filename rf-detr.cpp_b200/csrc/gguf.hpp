@@ -43,6 +43,9 @@ struct GgufTensor {
 
 struct GgufFile {
     uint32_t version = 0;
+    uint64_t n_kv = 0;
+    std::vector<uint8_t> kv_raw;    // the metadata section exactly as stored (for rewriting the file)
+    uint64_t alignment = 32;        // general.alignment
     std::unordered_map<std::string, GgufValue> kv;
     std::vector<GgufTensor> tensors;
     std::unordered_map<std::string, size_t> index;  // name -> tensors[]
@@ -58,6 +61,13 @@ struct GgufFile {
 // Parse the file.  Returns 0 on success, a negative rfdetr_status otherwise
 // (-2 file not found, -3 I/O, -6 malformed / unsupported format).
 int gguf_read(const std::string& path, GgufFile* out, std::string* err);
+
+// Write `f` as a GGUF file: the same version, metadata (kv_raw copied byte for
+// byte) and tensor order, tensor `i` of type tensors[i].type with its bytes at
+// f.data + tensors[i].offset; offsets are recomputed, every tensor's data is
+// aligned to f.alignment and zero-padded (the layout of gguf-py's GGUFWriter).
+// Returns 0 or a negative rfdetr_status (-3 I/O).
+int gguf_write(const std::string& path, const GgufFile& f, std::string* err);
 
 // Dequantize `n` elements of a tensor of type `t` to f32 (ggml's to_float
 // arithmetic for each block format).  Returns false for unsupported types.

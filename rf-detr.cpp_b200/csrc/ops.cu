@@ -4,6 +4,7 @@
 #include "gemm.cuh"
 #include "kernels.cuh"
 #include "mlp.cuh"
+#include "quant.cuh"
 #include "select.cuh"
 
 extern "C" int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int epi,
@@ -40,6 +41,12 @@ extern "C" int rfdetr_b200_op_attention(const void* q, const void* k, const void
     return (int)rfb::attention(static_cast<const __half*>(q), static_cast<const __half*>(k),
                                static_cast<const __half*>(v), ldq, ldk, ldv, static_cast<__half*>(o), ldo, seq_len,
                                groups, heads, head_dim, scale, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int rfdetr_b200_op_quantize(int type, const float* d_src, long long n, void* d_out, void* stream) {
+    if (!d_src || !d_out || n < 0) return (int)cudaErrorInvalidValue;
+    return (int)rfb::quantize_device((uint32_t)type, d_src, (int64_t)n, static_cast<uint8_t*>(d_out),
+                                     static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes, int batch, int nq, int nc,

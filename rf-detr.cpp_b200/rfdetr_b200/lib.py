@@ -45,7 +45,7 @@ class B200Det(C.Structure):
 
 
 class B200Params(C.Structure):
-    _fields_ = [("device", C.c_int), ("max_batch", C.c_int)]
+    _fields_ = [("device", C.c_int), ("max_batch", C.c_int), ("weight_type", C.c_int)]
 
 
 class ModelInfo(C.Structure):
@@ -119,6 +119,8 @@ SIGNATURES = {
     "rfdetr_b200_op_attention": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                            C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                            C.c_void_p]),
+    "rfdetr_b200_quantize_gguf": (C.c_int, [C.c_char_p, C.c_char_p, C.c_int, C.c_int]),
+    "rfdetr_b200_op_quantize": (C.c_int, [C.c_int, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
     "rfdetr_b200_op_select": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
                                         C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "rfdetr_b200_mask_bits_words": (C.c_size_t, [C.c_int, C.c_int]),
@@ -168,11 +170,12 @@ def _ptr(a):
 class Engine:
     """One rfdetr_context on one GPU (rfdetr_b200_init)."""
 
-    def __init__(self, model_path: str, device: int = 0, max_batch: int = 1):
+    def __init__(self, model_path: str, device: int = 0, max_batch: int = 1, weight_type: int = 0):
+        """weight_type: 0 = weights as stored, else re-quantize them at load (GGUF type id)."""
         L = lib()
         st = C.c_int(0)
         p = Params(model_path.encode(), 1, LOG_CB(), None)
-        b = B200Params(device, max_batch)
+        b = B200Params(device, max_batch, weight_type)
         self._ctx = L.rfdetr_b200_init(C.byref(p), C.byref(b), C.byref(st))
         if not self._ctx:
             raise RuntimeError(f"rfdetr_b200_init failed: {STATUS.get(st.value, st.value)} ({st.value})")
