@@ -162,24 +162,25 @@ def test_graph_replay_matches_direct_launches(make_model, monkeypatch):
 FULL = [("nano", "f16"), ("base", "q8_0"), ("medium", "q4_K"), ("seg-small", "f16"), ("large", "f16")]
 
 
-@pytest.mark.parametrize("variant,dtype", FULL)
-def test_full_size_configs(variant, dtype, make_model):
+def _check_variant(variant, dtype, batch, make_model):
+    """Engine vs oracle at the variant's full size: class scores and top-K,
+    then logits / boxes / masks with the oracle forced onto the engine's top-K."""
     import oracle as O
     from rfdetr_b200 import lib
 
     path = make_model(variant, dtype, 0)
     ora = O.Oracle(path)
-    eng = lib.Engine(path, max_batch=2)
+    eng = lib.Engine(path, max_batch=batch)
     S = eng.image_size
-    imgs = _images(S, 2, 500 + S)
+    imgs = _images(S, batch, 500 + S)
     lg, bx, mk = eng.forward_rgb(imgs)
     NQ, NC = eng.nq, eng.nc
     G = S // int(ora.meta["rfdetr.patch_size"])
-    topk = eng.trace("topk", 2).reshape(2, NQ).astype(np.int64)
-    cls_gpu = eng.trace("two_stage.cls_all", 2).reshape(2, G * G, NC)
+    topk = eng.trace("topk", batch).reshape(batch, NQ).astype(np.int64)
+    cls_gpu = eng.trace("two_stage.cls_all", batch).reshape(batch, G * G, NC)
     eng.close()
     tol = TOL[dtype]
-    for b in range(2):
+    for b in range(batch):
         x = ora.preprocess(imgs[b])
         own = ora.forward(x, trace=True)
         cls_o = own["trace"]["two_stage.cls_all"].reshape(G * G, NC)
@@ -190,6 +191,25 @@ def test_full_size_configs(variant, dtype, make_model):
         assert rel(bx[b], forced["boxes"]) < tol, (variant, b)
         if mk is not None:
             assert ((mk[b] > 0) == (forced["masks"] > 0)).mean() >= 0.99
+
+
+@pytest.mark.parametrize("variant,dtype", FULL)
+def test_full_size_configs(variant, dtype, make_model):
+    _check_variant(variant, dtype, 2, make_model)
+
+
+# The remaining variants of the converter's table (scripts/convert_rfdetr_to_gguf.py:125-205)
+# through the same kernels: Small; Seg-Nano (num_windows = 1: every block attends over the
+# whole 26 x 26 grid); Seg-Medium / Large; Seg-XLarge (G = 52) and Seg-2XLarge (G = 64, the
+# largest grid the top-K kernel takes), where the two-stage proposal mask fires
+# (src/two_stage.cpp:34-89).
+REST = [("small", "f16"), ("seg-nano", "f16"), ("seg-medium", "q8_0"), ("seg-large", "q4_K"),
+        ("seg-xlarge", "f16"), ("seg-2xlarge", "f16")]
+
+
+@pytest.mark.parametrize("variant,dtype", REST)
+def test_remaining_variants(variant, dtype, make_model):
+    _check_variant(variant, dtype, 1, make_model)
 
 
 def test_batch_position_invariance(make_model):
