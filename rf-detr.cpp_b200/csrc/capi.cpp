@@ -15,6 +15,7 @@
 #include "requant.hpp"
 #include "select.cuh"
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -183,6 +184,34 @@ void attach_names(const rfdetr_context* ctx, rfdetr_detection* d, size_t n) {
         if (d[i].class_id < names.size()) d[i].class_name = names[d[i].class_id].c_str();
 }
 
+// 0/255 byte masks from the device's bit masks: each byte of a mask word
+// becomes 8 output bytes through a 256-entry table of 8-byte patterns.
+struct MaskExpand {
+    uint64_t lut[256];
+    MaskExpand() {
+        for (int b = 0; b < 256; ++b) {
+            uint64_t v = 0;
+            for (int k = 0; k < 8; ++k)
+                if (b >> k & 1) v |= 0xFFull << (8 * k);
+            lut[b] = v;
+        }
+    }
+    void run(const uint32_t* bits, int w, int h, uint8_t* out) const {
+        const size_t wpr = (size_t)(w + 31) / 32;
+        for (int y = 0; y < h; ++y) {
+            const uint32_t* row = bits + y * wpr;
+            uint8_t* o = out + (size_t)y * w;
+            int x = 0;
+            for (; x + 8 <= w; x += 8) {
+                const uint64_t v = lut[(row[x >> 5] >> (x & 31)) & 0xFF];
+                std::memcpy(o + x, &v, 8);
+            }
+            for (; x < w; ++x) o[x] = (row[x >> 5] >> (x & 31)) & 1u ? 255 : 0;
+        }
+    }
+};
+const MaskExpand g_mask_expand;
+
 // Post-process the last forward of `batch` images of w x h pixels on the
 // device (select.cu) and build the per-image rfdetr_detection arrays: only the
 // selected records and their bit masks cross PCIe; the 0/255 masks of the
@@ -235,6 +264,8 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
         }
         if (RFB_CUDA_FAIL(cudaStreamSynchronize(st))) return RFDETR_ERR_INFERENCE;
     }
+    // masks to expand: (destination, bits) pairs, filled while building the records
+    std::vector<std::pair<uint8_t*, const uint32_t*>> jobs;
     size_t off = 0;
     for (int b = 0; b < batch; ++b) {
         const int n = ctx->h_counts[b];
@@ -250,13 +281,7 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
             d[i].x1 = r.x1; d[i].y1 = r.y1; d[i].x2 = r.x2; d[i].y2 = r.y2;
             if (seg) {
                 auto* m = static_cast<uint8_t*>(std::malloc((size_t)w * h));
-                if (m) {
-                    const uint32_t* src = ctx->h_bits + off + (size_t)i * words;
-                    const size_t wpr = (size_t)(w + 31) / 32;
-                    for (int y = 0; y < h; ++y)
-                        for (int x = 0; x < w; ++x)
-                            m[(size_t)y * w + x] = (src[y * wpr + (x >> 5)] >> (x & 31)) & 1u ? 255 : 0;
-                }
+                if (m) jobs.emplace_back(m, ctx->h_bits + off + (size_t)i * words);
                 d[i].mask = m;
                 d[i].mask_width = m ? w : 0;
                 d[i].mask_height = m ? h : 0;
@@ -266,6 +291,20 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
         attach_names(ctx, d, (size_t)n);
         out_dets[b] = d;
         out_counts[b] = (size_t)n;
+    }
+    // expand the masks, over the context's host threads when there is enough of it
+    const size_t pixels = jobs.size() * (size_t)w * h;
+    const int nt = (int)std::min<size_t>((size_t)ctx->n_threads, std::max<size_t>(1, pixels / (1u << 20)));
+    auto work = [&](int t) {
+        for (size_t j = (size_t)t; j < jobs.size(); j += (size_t)nt) g_mask_expand.run(jobs[j].second, w, h, jobs[j].first);
+    };
+    if (nt <= 1) {
+        work(0);
+    } else {
+        std::vector<std::thread> pool;
+        for (int t = 1; t < nt; ++t) pool.emplace_back(work, t);
+        work(0);
+        for (auto& th : pool) th.join();
     }
     return RFDETR_OK;
 }
