@@ -8,6 +8,7 @@
 #include "gemm.cuh"
 #include "kernels.cuh"
 #include "mlp.cuh"
+#include "sm100.cuh"
 
 #include <cmath>
 #include <cstdlib>
@@ -792,7 +793,12 @@ rfdetr_status Engine::finish() {
     int err = 0;
     if (RFB_CUDA_FAIL(cudaMemcpy(&err, d_err_, sizeof(int), cudaMemcpyDeviceToHost))) return RFDETR_ERR_INFERENCE;
     if (err) {
-        rfdetr_logf(RFDETR_LOG_ERROR, "forward: device error word %d (bounded wait expired)", err);
+        if ((err & 0xFF) == kErrWaitTimeout)
+            rfdetr_logf(RFDETR_LOG_ERROR,
+                        "forward: a kernel's bounded wait expired (mbarrier at shared offset 0x%x, cluster rank %d)",
+                        (unsigned)((err >> 8) & 0xFFFFF), (err >> 28) & 1);
+        else
+            rfdetr_logf(RFDETR_LOG_ERROR, "forward: device error word %d", err);
         cudaMemset(d_err_, 0, sizeof(int));
         return RFDETR_ERR_INFERENCE;
     }

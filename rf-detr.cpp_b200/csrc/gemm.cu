@@ -18,6 +18,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -29,18 +30,29 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 
-template <int BN, int EPI>
+#ifdef RFB_PAIR_DEBUG
+// progress counters of the two-SM path, read with rfdetr_b200_debug_pair (debug builds only)
+__device__ int g_pair_dbg[16];
+#define PAIR_DBG(i) atomicAdd(&g_pair_dbg[(i)], 1)
+#else
+#define PAIR_DBG(i) ((void)0)
+#endif
+
+template <int BN, int EPI, bool CTA2 = false>
 struct Cfg {
     // Two TMEM accumulators (epilogue of tile i overlaps the mainloop of tile
     // i+1) whenever 2 x BN columns fit in TMEM's 512; BN = 384 (full-row
     // LayerNorm of a 384-wide output) runs with one.
     static constexpr int NACC = 2 * BN <= 512 ? 2 : 1;
-    static constexpr int STAGES = BN > 256 ? 3 : (BN >= 192 ? 4 : (BN == 128 ? 6 : 8));
+    // CTA2: the tile is 256 x BN over a pair of SMs; this CTA holds its 128 A
+    // rows and half of the B rows, so its stages are smaller and more of them fit
+    static constexpr int B_ROWS = CTA2 ? BN / 2 : BN;
+    static constexpr int STAGES = CTA2 ? (BN >= 192 ? 6 : 8) : (BN > 256 ? 3 : (BN >= 192 ? 4 : (BN == 128 ? 6 : 8)));
     static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = NACC == 1 ? 512 : (BN == 192 ? 512 : 2 * BN);  // power of two
-    static constexpr int NSPLIT = BN > 256 ? 2 : 1;  // B tile in NSPLIT TMA boxes / MMAs of N <= 256
+    static constexpr int NSPLIT = B_ROWS > 256 ? 2 : 1;  // B tile in NSPLIT TMA boxes / MMAs of N <= 256
     static constexpr int OUT_STAGE = 8 * 4096;  // per epilogue warp: one 32-row x 128-byte box
     static constexpr int RED_BYTES = EPI == EPI_LN ? 1024 : 0;  // LN: per-row partial sums of 2 warps
     static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*align*/ + 256 /*barriers*/ + RED_BYTES;
@@ -53,11 +65,23 @@ constexpr int kEpiThreads = 256;  // warps 2..9
 // CONV: A is the implicit im2col of a 3x3 convolution (GemmArgs::conv_src);
 // a 128-row tile is conv_r whole image rows of one image, its rows past
 // conv_r * conv_w (and past the image) are computed but not stored.
-template <int BN, int EPI, int ACT, bool CONV = false>
+// CTA2: launched as clusters of two CTAs; each 256 x BN tile is computed by
+// tcgen05.mma.cta_group::2 issued by the pair's first CTA (rank 0).  Both
+// CTAs load their own 128 A rows and half of the B rows with ordinary TMA
+// onto their own barriers; every cross-CTA signal is a plain remote mbarrier
+// arrive, relayed by idle lanes of warp 0:
+//   rank 1 lane 1  "my half of stage s has landed"  -> rank 0's full[s] (count 2)
+//   rank 0 lane 1  "stage s consumed by the MMAs"   -> rank 1's empty[s]
+//   rank 0 lane 2  "accumulator buffer a is ready"  -> rank 1's tfull[a]
+//   epilogues of both CTAs "TMEM buffer a is free"  -> rank 0's tempty[a]
+// A relay cannot fall two phases behind: the next phase of the barrier it
+// watches needs the peer to have received the arrival it is about to send.
+template <int BN, int EPI, int ACT, bool CONV = false, bool CTA2 = false>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
        const __grid_constant__ CUtensorMap tmO16, const __grid_constant__ CUtensorMap tmO32, const GemmArgs p) {
-    using C = Cfg<BN, EPI>;
+    using C = Cfg<BN, EPI, CTA2>;
+    constexpr int TM = CTA2 ? 2 * BM : BM;  // rows per tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -76,7 +100,10 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
     const int lane = threadIdx.x & 31;
     // CONV: tiles per image (conv_r image rows each) x images
     const int conv_tpi = CONV ? (p.conv_h + p.conv_r - 1) / p.conv_r : 1;
-    const int m_tiles = CONV ? conv_tpi * (p.M / (p.conv_h * p.conv_w)) : (p.M + BM - 1) / BM;
+    const int m_tiles = CONV ? conv_tpi * (p.M / (p.conv_h * p.conv_w)) : (p.M + TM - 1) / TM;
+    const uint32_t rank = CTA2 ? cluster_ctarank() : 0u;
+    const int tile0 = CTA2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int tstep = CTA2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     const int n_tiles = (p.N + BN - 1) / BN;
     const int tiles_per_batch = m_tiles * n_tiles;
     const int num_tiles = tiles_per_batch * p.batches;
@@ -84,12 +111,12 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], CTA2 && rank == 0 ? 2 : 1);  // CTA2: own bytes + the peer's relay
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], kEpiThreads);
+            mbar_init(&tempty[a], CTA2 ? 2 * kEpiThreads : kEpiThreads);  // CTA2: both CTAs' epilogues
         }
         for (int q = 0; q < 4; ++q) mbar_init(&pairbar[q], 64);
         *cta_abort = 0;
@@ -99,9 +126,13 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
     }
-    if (warp == 1) tmem_alloc(tmem_holder, C::TMEM_COLS);
+    if (warp == 1) {
+        if constexpr (CTA2) tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
+        else tmem_alloc(tmem_holder, C::TMEM_COLS);
+    }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (CTA2) cluster_sync();  // the peer's barriers are initialised before any remote arrive
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
@@ -109,18 +140,23 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            for (int tile = tile0; tile < num_tiles; tile += tstep) {
                 const int b = tile / tiles_per_batch;
                 const int r = tile - b * tiles_per_batch;
                 const int mt = r / n_tiles, nt = r - mt * n_tiles;
-                const int arow = b * p.a_batch_rows + mt * BM;
-                const int brow = b * p.b_batch_rows + nt * BN;
+                const int arow = b * p.a_batch_rows + mt * TM + (int)rank * BM;
+                const int brow = b * p.b_batch_rows + nt * BN + (int)rank * C::B_ROWS;
                 const int cimg = CONV ? mt / conv_tpi : 0;
                 const int cy0 = CONV ? (mt - cimg * conv_tpi) * p.conv_r : 0;
                 const int cch = CONV ? p.conv_c / BK : 1;  // 64-channel chunks per tap
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, cta_abort, p.err)) goto done;
-                    if constexpr (CONV) {
+                    if constexpr (CTA2) {
+                        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);  // this CTA's half
+                        tma_load_2d(&tmA, &full[stage], sA + stage * C::A_BYTES, kb * BK, arow);
+                        tma_load_2d(&tmB, &full[stage], sB + stage * C::B_BYTES, kb * BK, brow);
+                        PAIR_DBG(0 + rank);
+                    } else if constexpr (CONV) {
                         // box (64 channels, conv_w pixels, conv_r rows) of the map shifted by the tap
                         const int tap = kb / cch, cc = kb - tap * cch;
                         mbar_arrive_expect_tx(&full[stage], C::B_BYTES + BK * 2 * p.conv_w * p.conv_r);
@@ -140,14 +176,38 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     }
                 }
             }
+        } else if (CTA2 && lane == 1) {
+            // k-block relay: rank 1 forwards "landed", rank 0 forwards "consumed"
+            int stage = 0;
+            uint32_t phase = 0;
+            uint64_t* watch = rank == 0 ? empty : full;
+            for (int tile = tile0; tile < num_tiles; tile += tstep) {
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&watch[stage], phase, cta_abort, p.err)) goto done;
+                    mbar_arrive_cluster(mapa_shared(smem_u32(&watch[stage]), rank ^ 1u));
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        } else if (CTA2 && lane == 2 && rank == 0) {
+            // accumulator relay: rank 0 forwards "ready" to rank 1
+            int local = 0;
+            for (int tile = tile0; tile < num_tiles; tile += tstep, ++local) {
+                const int acc = C::NACC == 2 ? (local & 1) : 0;
+                const uint32_t acc_phase = C::NACC == 2 ? ((local >> 1) & 1) : (local & 1);
+                if (!mbar_wait(&tfull[acc], acc_phase, cta_abort, p.err)) goto done;
+                mbar_arrive_cluster(mapa_shared(smem_u32(&tfull[acc]), 1u));
+            }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t IDESC = idesc_f16_f32(BM, BN / C::NSPLIT);
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t IDESC = idesc_f16_f32(TM, BN / C::NSPLIT);
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            for (int tile = tile0; tile < num_tiles; tile += tstep, ++local) {
                 const int acc = C::NACC == 2 ? (local & 1) : 0;
                 const uint32_t acc_phase = C::NACC == 2 ? ((local >> 1) & 1) : (local & 1);
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, cta_abort, p.err)) goto done;
@@ -155,24 +215,40 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(&full[stage], phase, cta_abort, p.err)) goto done;
+                    if (CTA2) PAIR_DBG(2);
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
                     const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
+                        if constexpr (CTA2) {
+                            umma_f16_pair(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32),
+                                          IDESC, (kb | kk) != 0);
+                        } else {
 #pragma unroll
-                        for (int sp = 0; sp < C::NSPLIT; ++sp)
-                            umma_f16(d_tmem + sp * (BN / C::NSPLIT), sw128_kmajor_desc(a0 + kk * 32),
-                                     sw128_kmajor_desc(b0 + sp * (BN / C::NSPLIT) * 128 + kk * 32), IDESC,
-                                     (kb | kk) != 0);
+                            for (int sp = 0; sp < C::NSPLIT; ++sp)
+                                umma_f16(d_tmem + sp * (BN / C::NSPLIT), sw128_kmajor_desc(a0 + kk * 32),
+                                         sw128_kmajor_desc(b0 + sp * (BN / C::NSPLIT) * 128 + kk * 32), IDESC,
+                                         (kb | kk) != 0);
+                        }
                     }
-                    umma_commit(&empty[stage]);
+                    if constexpr (CTA2) {
+                        umma_commit_pair(&empty[stage]);  // relayed to rank 1 by warp 0 lane 1
+                        PAIR_DBG(3);
+                    } else {
+                        umma_commit(&empty[stage]);
+                    }
                     if (++stage == C::STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
-                umma_commit(&tfull[acc]);
+                if constexpr (CTA2) {
+                    umma_commit_pair(&tfull[acc]);  // relayed to rank 1 by warp 0 lane 2
+                    PAIR_DBG(4);
+                } else {
+                    umma_commit(&tfull[acc]);
+                }
             }
         }
     } else {
@@ -191,7 +267,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         const int col_end = kSplit ? (half ? BN : kHalf0) : BN;
         int local = 0;
         uint32_t pair_phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        for (int tile = tile0; tile < num_tiles; tile += tstep, ++local) {
             const int b = tile / tiles_per_batch;
             const int r = tile - b * tiles_per_batch;
             const int mt = r / n_tiles, nt = r - mt * n_tiles;
@@ -207,9 +283,10 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 }
             }
             if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, cta_abort, p.err))) goto done;
+            if (CTA2 && warp == 2 && lane == 0) PAIR_DBG(5 + rank);
             tc_fence_after();
-            int m = mt * BM + row_in_tile;
-            const int m0w = mt * BM + quad * 32;
+            int m = mt * TM + (int)rank * BM + row_in_tile;
+            const int m0w = mt * TM + (int)rank * BM + quad * 32;
             bool row_ok = m < p.M;
             if constexpr (CONV) {
                 const int cimg = mt / conv_tpi, cy0 = (mt - cimg * conv_tpi) * p.conv_r;
@@ -524,15 +601,24 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            if constexpr (CTA2) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+            else mbar_arrive(&tempty[acc]);
         }
         if (lane == 0) bulk_wait<0>();
     }
 done:
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (CTA2) {
+        cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+        if (warp == 1) {
+            tc_fence_after();
+            tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+        }
+    } else {
+        __syncthreads();
+        if (warp == 1) {
+            tc_fence_after();
+            tmem_dealloc(tmem_base, C::TMEM_COLS);
+        }
     }
 }
 
@@ -597,7 +683,7 @@ bool make_conv_map(CUtensorMap* map, const void* base, int c, int w, int h, int 
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int EPI, int ACT, bool CONV = false>
+template <int BN, int EPI, int ACT, bool CONV = false, bool CTA2 = false>
 cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     GemmArgs a = a_in;
     static std::atomic<uint64_t> attr_set{0};  // per (BN, EPI) instantiation, one bit per device
@@ -606,8 +692,8 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_set.load() & bit)) {
-        e = cudaFuncSetAttribute(k_gemm<BN, EPI, ACT, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Cfg<BN, EPI>::SMEM);
+        e = cudaFuncSetAttribute(k_gemm<BN, EPI, ACT, CONV, CTA2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Cfg<BN, EPI, CTA2>::SMEM);
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
@@ -623,7 +709,8 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     } else if (!make_map(&ta, a.A, a.K, a_rows, a.lda, BM)) {
         return cudaErrorInvalidValue;
     }
-    if (!make_map(&tb, a.B, a.K, b_rows, a.ldb, BN / Cfg<BN, EPI>::NSPLIT)) return cudaErrorInvalidValue;
+    if (!make_map(&tb, a.B, a.K, b_rows, a.ldb, Cfg<BN, EPI, CTA2>::B_ROWS / Cfg<BN, EPI, CTA2>::NSPLIT))
+        return cudaErrorInvalidValue;
     CUtensorMap to16, to32;
     std::memset(&to16, 0, sizeof(to16));
     std::memset(&to32, 0, sizeof(to32));
@@ -631,16 +718,59 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     if (tma && a.out16) tma = make_out_map(&to16, a.out16, true, a.N, a.M, a.batches, a.ld16, a.out_batch_stride);
     if (tma && a.out32) tma = make_out_map(&to32, a.out32, false, a.N, a.M, a.batches, a.ld32, a.out_batch_stride);
     a.tma_out = tma ? 1 : 0;
+    constexpr int TM = CTA2 ? 2 * BM : BM;
     const int m_tiles = CONV ? ((a.conv_h + a.conv_r - 1) / a.conv_r) * (a.M / (a.conv_h * a.conv_w))
-                             : (a.M + BM - 1) / BM;
+                             : (a.M + TM - 1) / TM;
     const int tiles = m_tiles * ((a.N + BN - 1) / BN) * a.batches;
+    if constexpr (CTA2) {
+        // clusters of two CTAs, one cluster per pair of SMs (or per tile when there are fewer)
+        const int pairs = g_num_sms / 2;
+        const int grid = 2 * (tiles < pairs ? tiles : pairs);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = Cfg<BN, EPI, CTA2>::SMEM;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, k_gemm<BN, EPI, ACT, CONV, CTA2>, ta, tb, to16, to32, a);
+        if (e != cudaSuccess) return e;
+        return cudaGetLastError();
+    }
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
     k_gemm<BN, EPI, ACT, CONV><<<grid, kThreads, Cfg<BN, EPI>::SMEM, st>>>(ta, tb, to16, to32, a);
     return cudaGetLastError();
 }
 
+// Two-SM tiles (256 x BN over a cluster of two CTAs) for the large plain
+// GEMMs: f16 / f32 / residual epilogues, BN 192 or 256, one batch, and at
+// least two 256-row tiles per SM pair.  RFDETR_GEMM_2SM=0 keeps single-SM
+// tiles, =1 takes two-SM tiles for every eligible shape.
+bool use_pair(const GemmArgs& a, int bn) {
+    if (a.batches != 1 || (bn != 192 && bn != 256) || a.conv_src) return false;
+    if (a.epi != EPI_F16 && a.epi != EPI_F32 && a.epi != EPI_RESID) return false;
+    // opt-in: RFDETR_GEMM_2SM=1 forces pair tiles, =auto uses them when
+    // there are at least two pair-tiles per pair of SMs; default off
+    const char* env = std::getenv("RFDETR_GEMM_2SM");
+    if (!env || env[0] == '0') return false;
+    if (env[0] == '1') return true;
+    const long long tiles = (long long)((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + bn - 1) / bn);
+    return tiles >= (long long)g_num_sms;
+}
+
 template <int EPI, int ACT>
 cudaError_t dispatch_bn(const GemmArgs& a, int bn, cudaStream_t st) {
+    if constexpr (EPI == EPI_F16 || EPI == EPI_F32 || EPI == EPI_RESID) {
+        if (use_pair(a, bn)) {
+            if constexpr (ACT == ACT_NONE || ACT == ACT_GELU)
+                return bn == 256 ? launch<256, EPI, ACT, false, true>(a, st) : launch<192, EPI, ACT, false, true>(a, st);
+        }
+    }
     switch (bn) {
         case 256: return launch<256, EPI, ACT>(a, st);
         case 192: return launch<192, EPI, ACT>(a, st);
@@ -652,6 +782,20 @@ cudaError_t dispatch_bn(const GemmArgs& a, int bn, cudaStream_t st) {
 }  // namespace
 
 void gemm_set_num_sms(int n) { g_num_sms = n > 0 ? n : 148; }
+
+#ifdef RFB_PAIR_DEBUG
+}  // namespace rfb
+extern "C" int rfdetr_b200_debug_pair(int* host16, int reset) {
+    cudaDeviceSynchronize();
+    cudaMemcpyFromSymbol(host16, rfb::g_pair_dbg, 16 * sizeof(int));
+    if (reset) {
+        int z[16] = {};
+        cudaMemcpyToSymbol(rfb::g_pair_dbg, z, sizeof(z));
+    }
+    return 0;
+}
+namespace rfb {
+#endif
 
 cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
     if (!load_encode()) return cudaErrorNotSupported;
