@@ -48,6 +48,7 @@ struct Cfg {
     // rows and half of the B rows, so its stages are smaller and more of them fit
     static constexpr int B_ROWS = CTA2 ? BN / 2 : BN;
     static constexpr int STAGES = CTA2 ? (BN >= 192 ? 6 : 8) : (BN > 256 ? 3 : (BN >= 192 ? 4 : (BN == 128 ? 6 : 8)));
+    static_assert(!CTA2 || BN <= 256, "pair tiles: one MMA of N <= 256 over both CTAs' B halves");
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -66,16 +67,13 @@ constexpr int kEpiThreads = 256;  // warps 2..9
 // a 128-row tile is conv_r whole image rows of one image, its rows past
 // conv_r * conv_w (and past the image) are computed but not stored.
 // CTA2: launched as clusters of two CTAs; each 256 x BN tile is computed by
-// tcgen05.mma.cta_group::2 issued by the pair's first CTA (rank 0).  Both
-// CTAs load their own 128 A rows and half of the B rows with ordinary TMA
-// onto their own barriers; every cross-CTA signal is a plain remote mbarrier
-// arrive, relayed by idle lanes of warp 0:
-//   rank 1 lane 1  "my half of stage s has landed"  -> rank 0's full[s] (count 2)
-//   rank 0 lane 1  "stage s consumed by the MMAs"   -> rank 1's empty[s]
-//   rank 0 lane 2  "accumulator buffer a is ready"  -> rank 1's tfull[a]
-//   epilogues of both CTAs "TMEM buffer a is free"  -> rank 0's tempty[a]
-// A relay cannot fall two phases behind: the next phase of the barrier it
-// watches needs the peer to have received the arrival it is about to send.
+// tcgen05.mma.cta_group::2 issued by the pair's first CTA (rank 0):
+//   both producers   load their 128 A rows and BN/2 B rows; the bytes count on
+//                    rank 0's full[s] (expect_tx of both halves by rank 0)
+//   rank 0's MMA     commits "stage s consumed" to empty[s] and "accumulator a
+//                    ready" to tfull[a] of each CTA (one commit per CTA)
+//   both epilogues   arrive "TMEM buffer a free" on rank 0's tempty[a]
+// Barriers that the peer arrives on are waited with cluster-scope acquire.
 template <int BN, int EPI, int ACT, bool CONV = false, bool CTA2 = false>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -111,7 +109,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], CTA2 && rank == 0 ? 2 : 1);  // CTA2: own bytes + the peer's relay
+            mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -150,11 +148,12 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 const int cy0 = CONV ? (mt - cimg * conv_tpi) * p.conv_r : 0;
                 const int cch = CONV ? p.conv_c / BK : 1;  // 64-channel chunks per tap
                 for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1, cta_abort, p.err)) goto done;
+                    if (!mbar_wait<CTA2>(&empty[stage], phase ^ 1, cta_abort, p.err)) goto done;
                     if constexpr (CTA2) {
-                        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);  // this CTA's half
-                        tma_load_2d(&tmA, &full[stage], sA + stage * C::A_BYTES, kb * BK, arow);
-                        tma_load_2d(&tmB, &full[stage], sB + stage * C::B_BYTES, kb * BK, brow);
+                        if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);  // both halves
+                        const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+                        tma_load_2d_peer_bar(&tmA, fb, sA + stage * C::A_BYTES, kb * BK, arow);
+                        tma_load_2d_peer_bar(&tmB, fb, sB + stage * C::B_BYTES, kb * BK, brow);
                         PAIR_DBG(0 + rank);
                     } else if constexpr (CONV) {
                         // box (64 channels, conv_w pixels, conv_r rows) of the map shifted by the tap
@@ -166,39 +165,17 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
                         tma_load_2d(&tmA, &full[stage], sA + stage * C::A_BYTES, kb * BK, arow);
                     }
+                    if constexpr (!CTA2) {
 #pragma unroll
-                    for (int sp = 0; sp < C::NSPLIT; ++sp)
-                        tma_load_2d(&tmB, &full[stage], sB + stage * C::B_BYTES + sp * (BN / C::NSPLIT) * 128, kb * BK,
-                                    brow + sp * (BN / C::NSPLIT));
+                        for (int sp = 0; sp < C::NSPLIT; ++sp)
+                            tma_load_2d(&tmB, &full[stage], sB + stage * C::B_BYTES + sp * (BN / C::NSPLIT) * 128,
+                                        kb * BK, brow + sp * (BN / C::NSPLIT));
+                    }
                     if (++stage == C::STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
-            }
-        } else if (CTA2 && lane == 1) {
-            // k-block relay: rank 1 forwards "landed", rank 0 forwards "consumed"
-            int stage = 0;
-            uint32_t phase = 0;
-            uint64_t* watch = rank == 0 ? empty : full;
-            for (int tile = tile0; tile < num_tiles; tile += tstep) {
-                for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(&watch[stage], phase, cta_abort, p.err)) goto done;
-                    mbar_arrive_cluster(mapa_shared(smem_u32(&watch[stage]), rank ^ 1u));
-                    if (++stage == C::STAGES) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
-                }
-            }
-        } else if (CTA2 && lane == 2 && rank == 0) {
-            // accumulator relay: rank 0 forwards "ready" to rank 1
-            int local = 0;
-            for (int tile = tile0; tile < num_tiles; tile += tstep, ++local) {
-                const int acc = C::NACC == 2 ? (local & 1) : 0;
-                const uint32_t acc_phase = C::NACC == 2 ? ((local >> 1) & 1) : (local & 1);
-                if (!mbar_wait(&tfull[acc], acc_phase, cta_abort, p.err)) goto done;
-                mbar_arrive_cluster(mapa_shared(smem_u32(&tfull[acc]), 1u));
             }
         }
     } else if (warp == 1) {
@@ -210,11 +187,11 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
             for (int tile = tile0; tile < num_tiles; tile += tstep, ++local) {
                 const int acc = C::NACC == 2 ? (local & 1) : 0;
                 const uint32_t acc_phase = C::NACC == 2 ? ((local >> 1) & 1) : (local & 1);
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, cta_abort, p.err)) goto done;
+                if (!mbar_wait<CTA2>(&tempty[acc], acc_phase ^ 1, cta_abort, p.err)) goto done;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, cta_abort, p.err)) goto done;
+                    if (!mbar_wait<CTA2>(&full[stage], phase, cta_abort, p.err)) goto done;
                     if (CTA2) PAIR_DBG(2);
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
@@ -233,7 +210,8 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         }
                     }
                     if constexpr (CTA2) {
-                        umma_commit_pair(&empty[stage]);  // relayed to rank 1 by warp 0 lane 1
+                        umma_commit_pair(smem_u32(&empty[stage]));  // the stage is free in both CTAs
+                        umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
                         PAIR_DBG(3);
                     } else {
                         umma_commit(&empty[stage]);
@@ -244,7 +222,8 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     }
                 }
                 if constexpr (CTA2) {
-                    umma_commit_pair(&tfull[acc]);  // relayed to rank 1 by warp 0 lane 2
+                    umma_commit_pair(smem_u32(&tfull[acc]));  // both CTAs' accumulator halves are ready
+                    umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
                     PAIR_DBG(4);
                 } else {
                     umma_commit(&tfull[acc]);
@@ -282,7 +261,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     prefetch_l2_bulk(p.resid + (size_t)r0 * p.ldr, (uint32_t)nr * p.ldr * 4u);
                 }
             }
-            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, cta_abort, p.err))) goto done;
+            if (!__all_sync(0xffffffffu, mbar_wait<CTA2>(&tfull[acc], acc_phase, cta_abort, p.err))) goto done;
             if (CTA2 && warp == 2 && lane == 0) PAIR_DBG(5 + rank);
             tc_fence_after();
             int m = mt * TM + (int)rank * BM + row_in_tile;
@@ -499,21 +478,22 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         float bj[64];
                         load_cols<16>(bj, p.bias, n0, p.N, p.bias && n0 + 64 <= p.N && aligned16(p.bias + n0), 0.f);
                         tmem_wait_ld();
+                        // the whole chunk is computed before waiting for the previous bulk store
+                        // to release the staging box, so that wait overlaps the arithmetic
+                        uint32_t h[32];
+#pragma unroll
+                        for (int q = 0; q < 32; ++q) {
+                            const int jj = 2 * q;
+                            const float2 rv = make_float2(__uint_as_float(jj < 32 ? raw[jj] : raw2[jj - 32]),
+                                                          __uint_as_float(jj < 32 ? raw[jj + 1] : raw2[jj - 31]));
+                            const float2 w = act2<ACT>(__fadd2_rn(rv, make_float2(bj[jj], bj[jj + 1])));
+                            h[q] = pack_half2(w.x, w.y);
+                        }
                         if (lane == 0) bulk_wait_read<0>();
                         __syncwarp();
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            uint32_t h4[4];
-#pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const int jj = 8 * j + 2 * q;
-                                const float2 rv = make_float2(__uint_as_float(jj < 32 ? raw[jj] : raw2[jj - 32]),
-                                                              __uint_as_float(jj < 32 ? raw[jj + 1] : raw2[jj - 31]));
-                                const float2 w = act2<ACT>(__fadd2_rn(rv, make_float2(bj[jj], bj[jj + 1])));
-                                h4[q] = pack_half2(w.x, w.y);
-                            }
-                            st_shared_v4(swz(wbuf, lane, j), h4[0], h4[1], h4[2], h4[3]);
-                        }
+                        for (int j = 0; j < 8; ++j)
+                            st_shared_v4(swz(wbuf, lane, j), h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
                         fence_async_smem();
                         __syncwarp();
                         if (lane == 0) {
@@ -763,6 +743,13 @@ bool use_pair(const GemmArgs& a, int bn) {
     return tiles >= (long long)g_num_sms;
 }
 
+// Residual GEMMs of N = 384 and long K (the MLP's second linear) as one
+// 384-wide tile per row block; RFDETR_GEMM_BN384=0 falls back to two 192-wide tiles.
+bool wide_resid() {
+    const char* env = std::getenv("RFDETR_GEMM_BN384");
+    return !(env && env[0] == '0');
+}
+
 template <int EPI, int ACT>
 cudaError_t dispatch_bn(const GemmArgs& a, int bn, cudaStream_t st) {
     if constexpr (EPI == EPI_F16 || EPI == EPI_F32 || EPI == EPI_RESID) {
@@ -771,6 +758,8 @@ cudaError_t dispatch_bn(const GemmArgs& a, int bn, cudaStream_t st) {
                 return bn == 256 ? launch<256, EPI, ACT, false, true>(a, st) : launch<192, EPI, ACT, false, true>(a, st);
         }
     }
+    if constexpr (EPI == EPI_RESID && ACT == ACT_NONE)
+        if (bn == 384) return launch<384, EPI, ACT>(a, st);
     switch (bn) {
         case 256: return launch<256, EPI, ACT>(a, st);
         case 192: return launch<192, EPI, ACT>(a, st);
@@ -823,6 +812,8 @@ cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
         if (a.N != 128 && a.N != 256 && a.N != 384) return cudaErrorInvalidValue;
         if (!a.ln_g || !a.ln_b) return cudaErrorInvalidValue;
         bn = a.N;
+    } else if (a.N == 384 && a.epi == EPI_RESID && a.act == ACT_NONE && a.K >= 768 && wide_resid()) {
+        bn = 384;  // one full-row tile: A crosses from L2 once per row block instead of twice
     } else if (a.N % 256 == 0) {
         bn = 256;
     } else if (a.N % 192 == 0) {

@@ -43,15 +43,28 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// kCluster: acquire at cluster scope, for barriers that CTAs of the cluster
+// other than this one arrive on
+template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
+    if constexpr (kCluster) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+    }
     return ok != 0;
 }
 
@@ -66,11 +79,12 @@ __device__ __forceinline__ int wait_error_word(const uint64_t* bar) {
 // Bounded wait on an mbarrier phase.  Returns false (after recording the
 // error) if the phase did not complete within kWaitLimitNs or another role
 // of the CTA already aborted.
+template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* cta_abort, int* err) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<kCluster>(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait<kCluster>(bar, parity)) return true;
         if (*cta_abort) return false;
         if (globaltimer() - t0 > kWaitLimitNs) {
             *cta_abort = 1;
@@ -207,11 +221,21 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, u
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// Arrive on this CTA's mbarrier `bar` once the pair MMAs issued so far by
-// this thread are done.
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
+// Arrive on the mbarrier at shared::cluster address `bar` (this CTA's or the
+// peer's, see mapa_shared) once the pair MMAs issued so far by this thread are done.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 2-D tiled TMA load into this CTA's shared memory whose byte count completes
+// on the mbarrier at shared::cluster address `bar`, which may be the peer
+// CTA's of the pair (used to count both CTAs' operand halves on one barrier).
+__device__ __forceinline__ void tma_load_2d_peer_bar(const CUtensorMap* map, uint32_t bar, void* dst, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(bar), "r"(x), "r"(y)
+        : "memory");
 }
 // Plain arrive on an mbarrier given by cluster address (possibly the peer CTA's).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {

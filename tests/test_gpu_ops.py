@@ -33,7 +33,7 @@ def rel(a, b):
 
 
 GEMM_SHAPES = [(300, 256, 256), (1000, 1152, 384), (517, 91, 256), (200, 4, 256), (4097, 1536, 384),
-               (333, 384, 1536), (129, 256, 592), (64, 512, 512), (2000, 2048, 256), (1, 128, 64)]
+               (333, 384, 1536), (4097, 384, 768), (129, 256, 592), (64, 512, 512), (2000, 2048, 256), (1, 128, 64)]
 
 
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
