@@ -47,6 +47,8 @@ struct Cfg {
     // CTA2: the tile is 256 x BN over a pair of SMs; this CTA holds its 128 A
     // rows and half of the B rows, so its stages are smaller and more of them fit
     static constexpr int B_ROWS = CTA2 ? BN / 2 : BN;
+    static constexpr int NEPI = 8;  // epilogue warps: two per TMEM lane quadrant
+    static constexpr int THREADS = 64 + 32 * NEPI;
     static constexpr int STAGES = CTA2 ? (BN >= 192 ? 6 : 8) : (BN > 256 ? 3 : (BN >= 192 ? 4 : (BN == 128 ? 6 : 8)));
     static_assert(!CTA2 || BN <= 256, "pair tiles: one MMA of N <= 256 over both CTAs' B halves");
     static constexpr int A_BYTES = BM * BK * 2;
@@ -54,14 +56,12 @@ struct Cfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = NACC == 1 ? 512 : (BN == 192 ? 512 : 2 * BN);  // power of two
     static constexpr int NSPLIT = B_ROWS > 256 ? 2 : 1;  // B tile in NSPLIT TMA boxes / MMAs of N <= 256
-    static constexpr int OUT_STAGE = 8 * 4096;  // per epilogue warp: one 32-row x 128-byte box
+    static constexpr int OUT_STAGE = NEPI * 4096;  // per epilogue warp: one 32-row x 128-byte box
     static constexpr int RED_BYTES = EPI == EPI_LN ? 1024 : 0;  // LN: per-row partial sums of 2 warps
     static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*align*/ + 256 /*barriers*/ + RED_BYTES;
     static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-constexpr int kThreads = 320;     // 10 warps
-constexpr int kEpiThreads = 256;  // warps 2..9
 
 // CONV: A is the implicit im2col of a 3x3 convolution (GemmArgs::conv_src);
 // a 128-row tile is conv_r whole image rows of one image, its rows past
@@ -75,7 +75,7 @@ constexpr int kEpiThreads = 256;  // warps 2..9
 //   both epilogues   arrive "TMEM buffer a free" on rank 0's tempty[a]
 // Barriers that the peer arrives on are waited with cluster-scope acquire.
 template <int BN, int EPI, int ACT, bool CONV = false, bool CTA2 = false>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<BN, EPI, CTA2>::THREADS, 1)
 k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
        const __grid_constant__ CUtensorMap tmO16, const __grid_constant__ CUtensorMap tmO32, const GemmArgs p) {
     using C = Cfg<BN, EPI, CTA2>;
@@ -114,7 +114,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], CTA2 ? 2 * kEpiThreads : kEpiThreads);  // CTA2: both CTAs' epilogues
+            mbar_init(&tempty[a], (CTA2 ? 2 : 1) * 32 * C::NEPI);  // CTA2: both CTAs' epilogues
         }
         for (int q = 0; q < 4; ++q) mbar_init(&pairbar[q], 64);
         *cta_abort = 0;
@@ -665,6 +665,7 @@ bool make_conv_map(CUtensorMap* map, const void* base, int c, int w, int h, int 
 
 template <int BN, int EPI, int ACT, bool CONV = false, bool CTA2 = false>
 cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
+    using C = Cfg<BN, EPI, CTA2>;
     GemmArgs a = a_in;
     static std::atomic<uint64_t> attr_set{0};  // per (BN, EPI) instantiation, one bit per device
     int dev = 0;
@@ -673,7 +674,7 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_set.load() & bit)) {
         e = cudaFuncSetAttribute(k_gemm<BN, EPI, ACT, CONV, CTA2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Cfg<BN, EPI, CTA2>::SMEM);
+                                 C::SMEM);
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
@@ -689,7 +690,7 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     } else if (!make_map(&ta, a.A, a.K, a_rows, a.lda, BM)) {
         return cudaErrorInvalidValue;
     }
-    if (!make_map(&tb, a.B, a.K, b_rows, a.ldb, Cfg<BN, EPI, CTA2>::B_ROWS / Cfg<BN, EPI, CTA2>::NSPLIT))
+    if (!make_map(&tb, a.B, a.K, b_rows, a.ldb, C::B_ROWS / C::NSPLIT))
         return cudaErrorInvalidValue;
     CUtensorMap to16, to32;
     std::memset(&to16, 0, sizeof(to16));
@@ -708,8 +709,8 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
         const int grid = 2 * (tiles < pairs ? tiles : pairs);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)grid);
-        cfg.blockDim = dim3(kThreads);
-        cfg.dynamicSmemBytes = Cfg<BN, EPI, CTA2>::SMEM;
+        cfg.blockDim = dim3(C::THREADS);
+        cfg.dynamicSmemBytes = C::SMEM;
         cfg.stream = st;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -723,7 +724,7 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
         return cudaGetLastError();
     }
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-    k_gemm<BN, EPI, ACT, CONV><<<grid, kThreads, Cfg<BN, EPI>::SMEM, st>>>(ta, tb, to16, to32, a);
+    k_gemm<BN, EPI, ACT, CONV><<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, to16, to32, a);
     return cudaGetLastError();
 }
 
@@ -822,6 +823,12 @@ cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
         bn = 128;
     } else {
         bn = 64;
+    }
+    if (a.epi != EPI_LN) {
+        // tuning override: RFDETR_GEMM_BN = 128 / 192 / 256 where it divides N
+        const char* env = std::getenv("RFDETR_GEMM_BN");
+        const int f = env ? std::atoi(env) : 0;
+        if ((f == 128 || f == 192 || f == 256) && a.N % f == 0) bn = f;
     }
     // instantiated (epilogue, activation) pairs
     switch (a.epi) {
