@@ -83,56 +83,86 @@ __global__ void k_patch_im2col(const float* __restrict__ img, int B, int S, int 
 // Preprocess (src/image_io.cpp:207-248) fused into the patch im2col: each
 // im2col element is one normalized model-resolution pixel, sampled straight
 // from the uint8 source with the same double-precision source coordinates.
-// One thread per (patch, channel, kernel row): p consecutive outputs, so the
-// index arithmetic is paid once per p elements.
-__global__ void k_patch_from_rgb(const uint8_t* __restrict__ rgb, int B, int w, int h, int S, int p, int nw, int Kpad,
-                                 float m0, float m1, float m2, float s0, float s1, float s2, __half* __restrict__ A) {
+// One thread per 8 consecutive im2col elements of a row (one 16-byte store):
+// element k of a row is (channel, kernel row, kernel column) =
+// (k / p^2, k / p mod p, k mod p); elements past 3 p^2 are the zero K padding.
+// Without resizing, every element is (u / 255 - mean_c) / std_c of a source
+// byte u: a per-block table of those 768 floats (the same float expression)
+// replaces the two divisions per element.
+__global__ void __launch_bounds__(256) k_patch_from_rgb(const uint8_t* __restrict__ rgb, int B, int w, int h, int S,
+                                                        int p, int nw, int Kpad, float m0, float m1, float m2,
+                                                        float s0, float s1, float s2, __half* __restrict__ A) {
+    __shared__ float lut[3 * 256];
+    const bool identity = w == S && h == S;
+    if (identity) {
+        for (int t = threadIdx.x; t < 3 * 256; t += blockDim.x) {
+            const int cc = t >> 8;
+            const float mean = cc == 0 ? m0 : (cc == 1 ? m1 : m2), sd = cc == 0 ? s0 : (cc == 1 ? s1 : s2);
+            lut[t] = ((float)(t & 255) / 255.0f - mean) / sd;
+        }
+        __syncthreads();
+    }
     const int G = S / p, ws = G / nw, Tp = ws * ws;
-    const int segs = 3 * p;  // (channel, ky) segments per patch
+    const int chunks = Kpad / 8;
     const size_t rows = (size_t)B * nw * nw * Tp;
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= rows * segs + rows) return;
-    if (i >= rows * segs) {  // zero the K padding of one row
-        const size_t row = i - rows * segs;
-        for (int k = 3 * p * p; k < Kpad; ++k) A[row * Kpad + k] = __float2half_rn(0.f);
-        return;
-    }
-    const size_t row = i / segs;
-    const int seg = (int)(i - row * segs);
-    const int c = seg / p, ky = seg - c * p;
+    if (i >= rows * chunks) return;
+    const size_t row = i / chunks;
+    const int k0 = (int)(i - row * chunks) * 8;
     const int b = (int)(row / ((size_t)nw * nw * Tp));
     const int rr = (int)(row - (size_t)b * nw * nw * Tp);
     const int win = rr / Tp, t = rr - win * Tp;
     const int gy = (win / nw) * ws + t / ws, gx = (win % nw) * ws + t % ws;
-    const int yy = gy * p + ky, x0p = gx * p;
-    const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2), sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
     const uint8_t* img = rgb + (size_t)b * h * w * 3;
-    __half* dst = A + row * Kpad + (size_t)(c * p + ky) * p;
-    if (w == S && h == S) {
-        // identity resize: source coordinate == destination, interpolation weights 0
-        const uint8_t* src = img + ((size_t)yy * w + x0p) * 3 + c;
-        for (int kx = 0; kx < p; ++kx) dst[kx] = __float2half_rn(((float)src[kx * 3] / 255.0f - mean) / sd);
-        return;
-    }
+    const int kreal = 3 * p * p;
+    int c = k0 / (p * p);
+    int ky = (k0 - c * p * p) / p;
+    int kx = k0 - c * p * p - ky * p;
     const double scx = (double)w / (double)S, scy = (double)h / (double)S;
-    const double fy = ((double)yy + 0.5) * scy - 0.5;
-    const int y0r = (int)floor(fy);
-    const int y0 = min(max(y0r, 0), h - 1), y1 = min(max(y0r + 1, 0), h - 1);
-    const float wy = (float)(fy - (double)y0r);
-    for (int kx = 0; kx < p; ++kx) {
-        const int xx = x0p + kx;
-        const double fx = ((double)xx + 0.5) * scx - 0.5;
-        const int x0r = (int)floor(fx);
-        const int x0 = min(max(x0r, 0), w - 1), x1 = min(max(x0r + 1, 0), w - 1);
-        const float wx = (float)(fx - (double)x0r);
-        const float p00 = (float)img[((size_t)y0 * w + x0) * 3 + c];
-        const float p01 = (float)img[((size_t)y0 * w + x1) * 3 + c];
-        const float p10 = (float)img[((size_t)y1 * w + x0) * 3 + c];
-        const float p11 = (float)img[((size_t)y1 * w + x1) * 3 + c];
-        const float top = p00 + (p01 - p00) * wx;
-        const float bot = p10 + (p11 - p10) * wx;
-        dst[kx] = __float2half_rn(((top + (bot - top) * wy) / 255.0f - mean) / sd);
+    uint32_t out[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        float v2[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            float v = 0.f;
+            if (k0 + e + u < kreal) {
+                const int yy = gy * p + ky, xx = gx * p + kx;
+                if (identity) {
+                    // identity resize: source coordinate == destination, interpolation weights 0
+                    v = lut[(c << 8) + img[((size_t)yy * w + xx) * 3 + c]];
+                } else {
+                    const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2), sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+                    const double fy = ((double)yy + 0.5) * scy - 0.5;
+                    const int y0r = (int)floor(fy);
+                    const int y0 = min(max(y0r, 0), h - 1), y1 = min(max(y0r + 1, 0), h - 1);
+                    const float wy = (float)(fy - (double)y0r);
+                    const double fx = ((double)xx + 0.5) * scx - 0.5;
+                    const int x0r = (int)floor(fx);
+                    const int x0 = min(max(x0r, 0), w - 1), x1 = min(max(x0r + 1, 0), w - 1);
+                    const float wx = (float)(fx - (double)x0r);
+                    const float p00 = (float)img[((size_t)y0 * w + x0) * 3 + c];
+                    const float p01 = (float)img[((size_t)y0 * w + x1) * 3 + c];
+                    const float p10 = (float)img[((size_t)y1 * w + x0) * 3 + c];
+                    const float p11 = (float)img[((size_t)y1 * w + x1) * 3 + c];
+                    const float top = p00 + (p01 - p00) * wx;
+                    const float bot = p10 + (p11 - p10) * wx;
+                    v = ((top + (bot - top) * wy) / 255.0f - mean) / sd;
+                }
+            }
+            v2[u] = v;
+            if (++kx == p) {
+                kx = 0;
+                if (++ky == p) {
+                    ky = 0;
+                    ++c;
+                }
+            }
+        }
+        __half2 hv = __floats2half2_rn(v2[0], v2[1]);
+        out[e >> 1] = *reinterpret_cast<uint32_t*>(&hv);
     }
+    *reinterpret_cast<uint4*>(A + row * Kpad + k0) = make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 __global__ void k_cls_rows(float* __restrict__ x, const float* __restrict__ clsrow, int B, int NW, int T, int D) {
@@ -183,12 +213,29 @@ __global__ void k_layernorm(const float* x, int rows, int D, const float* __rest
 // Grid-stride over rows (one warp per row at a time); the next row's loads are
 // issued before the current row's reductions so each warp keeps two rows of
 // loads in flight.
-template <int NV>
+// TAP = false: row r of the output normalises row r of x (contiguous
+// outputs).  TAP = true, the backbone tap: output r is grid pixel (b, gy, gx)
+// in row-major order, read from its windowed token (window-major, a CLS row
+// first in each window) and written at column col0 of an f16 row of pitch ld.
+struct TapMap {
+    int G = 0, nw = 1, ld = 0, col0 = 0;
+    __device__ __forceinline__ size_t src_row(int r) const {
+        const int b = r / (G * G), pix = r - b * G * G;
+        const int gy = pix / G, gx = pix - gy * G;
+        const int ws = G / nw, T = ws * ws + 1;
+        const int win = (gy / ws) * nw + gx / ws;
+        return (size_t)b * nw * nw * T + win * T + 1 + (gy % ws) * ws + gx % ws;
+    }
+};
+
+template <int NV, bool TAP = false>
 __global__ void __launch_bounds__(256) k_layernorm_v4(const float* x, int rows, const float* __restrict__ g,
                                                      const float* __restrict__ b, float eps, float* y32,
-                                                     __half* __restrict__ y16) {
+                                                     __half* __restrict__ y16, TapMap tm) {
     constexpr int D = 128 * NV;
     const int lane = threadIdx.x & 31;
+    const size_t ld16 = TAP ? (size_t)tm.ld : (size_t)D;
+    const int col0 = TAP ? tm.col0 : 0;
     const int stride = gridDim.x * (blockDim.x >> 5);
     int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -200,13 +247,15 @@ __global__ void __launch_bounds__(256) k_layernorm_v4(const float* x, int rows, 
     }
     float4 v[NV];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) v[i] = reinterpret_cast<const float4*>(x + (size_t)row * D)[lane + 32 * i];
+    for (int i = 0; i < NV; ++i)
+        v[i] = reinterpret_cast<const float4*>(x + (TAP ? tm.src_row(row) : (size_t)row) * D)[lane + 32 * i];
     for (; row < rows; row += stride) {
         const int nxt = row + stride;
         float4 vn[NV];
         if (nxt < rows) {
+            const float4* xn = reinterpret_cast<const float4*>(x + (TAP ? tm.src_row(nxt) : (size_t)nxt) * D);
 #pragma unroll
-            for (int i = 0; i < NV; ++i) vn[i] = reinterpret_cast<const float4*>(x + (size_t)nxt * D)[lane + 32 * i];
+            for (int i = 0; i < NV; ++i) vn[i] = xn[lane + 32 * i];
         }
         float s = 0.f;
 #pragma unroll
@@ -233,7 +282,7 @@ __global__ void __launch_bounds__(256) k_layernorm_v4(const float* x, int rows, 
                 uint2 u;
                 u.x = *reinterpret_cast<uint32_t*>(&h0);
                 u.y = *reinterpret_cast<uint32_t*>(&h1);
-                *reinterpret_cast<uint2*>(y16 + (size_t)row * D + c0) = u;
+                *reinterpret_cast<uint2*>(y16 + (size_t)row * ld16 + col0 + c0) = u;
             }
         }
         if (nxt < rows) {
@@ -596,7 +645,8 @@ cudaError_t patch_from_rgb(const uint8_t* rgb, int B, int w, int h, int S, int p
                            const float* mean3, const float* std3, __half* A, cudaStream_t st) {
     const int G = S / p, Tp = (G / nw) * (G / nw);
     const size_t rows = (size_t)B * nw * nw * Tp;
-    const size_t n = rows * 3 * p + rows;
+    if (Kpad % 8 || Kpad < 3 * p * p || ((uintptr_t)A & 15)) return cudaErrorInvalidValue;  // 16-byte stores
+    const size_t n = rows * (Kpad / 8);
     k_patch_from_rgb<<<cdiv(n, 256), 256, 0, st>>>(rgb, B, w, h, S, p, nw, Kpad, mean3[0], mean3[1], mean3[2],
                                                    std3[0], std3[1], std3[2], A);
     return cudaGetLastError();
@@ -615,8 +665,8 @@ cudaError_t layernorm(const float* x, int rows, int D, const float* g, const flo
     const bool vec = (D % 128 == 0) && !(((uintptr_t)x | (uintptr_t)y32 | (uintptr_t)y16) & 15);
     // the vector kernel is grid-strided: a few resident blocks per SM
     const unsigned vblocks = blocks < (unsigned)(148 * 6) ? blocks : (unsigned)(148 * 6);
-    if (vec && D == 384) k_layernorm_v4<3><<<vblocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16);
-    else if (vec && D == 256) k_layernorm_v4<2><<<vblocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16);
+    if (vec && D == 384) k_layernorm_v4<3><<<vblocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16, TapMap{});
+    else if (vec && D == 256) k_layernorm_v4<2><<<vblocks, 256, 0, st>>>(x, rows, g, b, eps, y32, y16, TapMap{});
     else if (D <= 256) k_layernorm<8><<<blocks, 256, 0, st>>>(x, rows, D, g, b, eps, y32, y16);
     else k_layernorm<16><<<blocks, 256, 0, st>>>(x, rows, D, g, b, eps, y32, y16);
     return cudaGetLastError();
@@ -625,7 +675,18 @@ cudaError_t layernorm(const float* x, int rows, int D, const float* g, const flo
 cudaError_t backbone_tap(const float* x, int B, int G, int nw, int D, const float* g, const float* b, __half* taps,
                          int ld, int col0, cudaStream_t st) {
     if (D > 384) return cudaErrorInvalidValue;
-    k_tap<<<cdiv((size_t)B * G * G, 8), 256, 0, st>>>(x, B, G, nw, D, g, b, taps, ld, col0);
+    const int rows = B * G * G;
+    if ((D == 384 || D == 256) && ld % 4 == 0 && col0 % 4 == 0 && !(((uintptr_t)x | (uintptr_t)taps) & 15) &&
+        !(((uintptr_t)g | (uintptr_t)b) & 15)) {
+        // vectorised, grid-strided LayerNorm over the gathered rows (8-byte f16 stores)
+        TapMap tm;
+        tm.G = G; tm.nw = nw; tm.ld = ld; tm.col0 = col0;
+        const unsigned blocks = cdiv(rows, 8) < (unsigned)(148 * 6) ? cdiv(rows, 8) : (unsigned)(148 * 6);
+        if (D == 384) k_layernorm_v4<3, true><<<blocks, 256, 0, st>>>(x, rows, g, b, 1e-6f, nullptr, taps, tm);
+        else k_layernorm_v4<2, true><<<blocks, 256, 0, st>>>(x, rows, g, b, 1e-6f, nullptr, taps, tm);
+        return cudaGetLastError();
+    }
+    k_tap<<<cdiv((size_t)rows, 8), 256, 0, st>>>(x, B, G, nw, D, g, b, taps, ld, col0);
     return cudaGetLastError();
 }
 

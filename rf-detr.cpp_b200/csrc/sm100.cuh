@@ -193,6 +193,16 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
         : "memory");
 }
 
+// Two warps (64 threads, e.g. the two that share a TMEM lane quadrant) meet
+// at the mbarrier `bar` (initialised with count 64); bounded like every other
+// wait.  Returns false (warp-uniformly) when the CTA is unwinding.
+__device__ __forceinline__ bool pair_sync(uint64_t* bar, uint32_t& phase, volatile int* cta_abort, int* err) {
+    mbar_arrive(bar);
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, phase, cta_abort, err));
+    phase ^= 1;
+    return ok;
+}
+
 // ---- two-SM (cta_group::2) pairs: a cluster of two CTAs shares each MMA ----
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

@@ -163,12 +163,38 @@ def test_fused_mlp(M, D, FH, with_ls):
 
 
 @pytest.mark.parametrize("L,groups,heads,hd", [(101, 8, 6, 64), (580, 2, 6, 64), (1616, 1, 6, 64),
-                                               (300, 3, 8, 32), (17, 5, 6, 64), (64, 2, 8, 32)])
+                                               (300, 3, 8, 32), (17, 5, 6, 64), (64, 2, 8, 32),
+                                               (150, 3, 6, 64), (129, 2, 6, 64), (256, 2, 6, 64)])
 def test_attention(L, groups, heads, hd):
     torch.manual_seed(L + groups)
     dev = "cuda:0"
     D = heads * hd
     qkv = torch.randn(groups * L, 3 * D, device=dev).half()
+    o = torch.zeros(groups * L, D, dtype=torch.float16, device=dev)
+    scale = 1.0 / math.sqrt(hd)
+    rc = _lib().rfdetr_b200_op_attention(_p(qkv), _p(qkv[:, D:]), _p(qkv[:, 2 * D:]), 3 * D, 3 * D, 3 * D, _p(o), D,
+                                         L, groups, heads, hd, scale, _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    x = qkv.double().view(groups, L, 3, heads, hd)
+    q, k, v = x[:, :, 0].transpose(1, 2), x[:, :, 1].transpose(1, 2), x[:, :, 2].transpose(1, 2)
+    ref = torch.softmax(q @ k.transpose(-1, -2) * scale, -1) @ v
+    ref = ref.transpose(1, 2).reshape(groups * L, D)
+    assert rel(o, ref) < 4e-3
+
+
+@pytest.mark.parametrize("L", [1616, 150, 700])
+def test_attention_growing_max(L):
+    """Scores whose row maximum keeps growing along the keys, so the lazily
+    raised reference max moves several times and O is rescaled in TMEM."""
+    torch.manual_seed(L)
+    dev = "cuda:0"
+    groups, heads, hd = 2, 6, 64
+    D = heads * hd
+    qkv = torch.randn(groups * L, 3 * D, device=dev)
+    ramp = torch.linspace(0.2, 3.0, L, device=dev).repeat(groups)[:, None]
+    qkv[:, D:2 * D] *= ramp  # later keys score higher: the block maxima rise by several log2 units
+    qkv = qkv.half()
     o = torch.zeros(groups * L, D, dtype=torch.float16, device=dev)
     scale = 1.0 / math.sqrt(hd)
     rc = _lib().rfdetr_b200_op_attention(_p(qkv), _p(qkv[:, D:]), _p(qkv[:, 2 * D:]), 3 * D, 3 * D, 3 * D, _p(o), D,
