@@ -42,6 +42,21 @@ rfdetr_context* rfdetr_b200_init(const rfdetr_params* params, const rfdetr_b200_
 rfdetr_status rfdetr_b200_forward_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width, int height,
                                       float* out_logits, float* out_boxes, float* out_masks);
 
+/* Pipelined form of rfdetr_b200_forward_rgb for a stream of batches: enqueues
+ * the host-to-device copy of `rgb` (on a copy stream, into one of two device
+ * input slots), the forward (behind that copy) and the device-to-host copies
+ * of the outputs, and returns without waiting, so the upload of the next batch
+ * overlaps the forward of this one.  `rgb` and the output buffers must stay
+ * valid and untouched until rfdetr_b200_wait returns; page-locked host memory
+ * is needed for the copies to overlap (pageable memory works, serialized).
+ * Outputs as for rfdetr_b200_forward_rgb. */
+rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width, int height,
+                                     float* out_logits, float* out_boxes, float* out_masks);
+
+/* Waits for every rfdetr_b200_submit_rgb issued so far; reports device errors
+ * of any of them. */
+rfdetr_status rfdetr_b200_wait(rfdetr_context* ctx);
+
 /* Same, from already-preprocessed planar input [batch][3][S][S] (S = image
  * size), i.e. exactly the `input` argument of rfdetr_model_forward. */
 rfdetr_status rfdetr_b200_forward_planar(rfdetr_context* ctx, const float* planar, int batch,

@@ -46,6 +46,15 @@ struct rfdetr_context {
     int* h_counts = nullptr;
     uint32_t* h_bits = nullptr;
     size_t h_dets_cap = 0, h_counts_cap = 0, h_bits_cap = 0;
+    // pipelined submissions (rfdetr_b200_submit_rgb): two device input slots
+    // filled on a copy stream; the forward and the output copies run on the
+    // engine stream behind slot_ready, and slot_free marks the slot's last reader
+    cudaStream_t copy_stream = nullptr;
+    uint8_t* d_slot[2] = {nullptr, nullptr};
+    size_t slot_cap[2] = {0, 0};
+    cudaEvent_t slot_ready[2] = {nullptr, nullptr};
+    cudaEvent_t slot_free[2] = {nullptr, nullptr};
+    int next_slot = 0;
 
     ~rfdetr_context() {
         if (h_in) cudaFreeHost(h_in);
@@ -54,6 +63,14 @@ struct rfdetr_context {
         if (h_counts) cudaFreeHost(h_counts);
         if (h_bits) cudaFreeHost(h_bits);
         if (engine) cudaSetDevice(engine->device());
+        if (copy_stream) cudaStreamSynchronize(copy_stream);
+        if (engine) cudaStreamSynchronize(engine->stream());
+        for (int k = 0; k < 2; ++k) {
+            if (d_slot[k]) cudaFree(d_slot[k]);
+            if (slot_ready[k]) cudaEventDestroy(slot_ready[k]);
+            if (slot_free[k]) cudaEventDestroy(slot_free[k]);
+        }
+        if (copy_stream) cudaStreamDestroy(copy_stream);
         if (d_dets) cudaFree(d_dets);
         if (d_counts) cudaFree(d_counts);
         if (d_filter) cudaFree(d_filter);
@@ -145,7 +162,8 @@ rfdetr_context* init_impl(const rfdetr_params* params, int device, int max_batch
 }
 
 // Copy the last forward's outputs for `batch` images to host buffers.
-rfdetr_status fetch_outputs(rfdetr_context* ctx, int batch, float* logits, float* boxes, float* masks) {
+// Enqueue the device-to-host copies of the outputs on the engine stream.
+rfdetr_status enqueue_output_copies(rfdetr_context* ctx, int batch, float* logits, float* boxes, float* masks) {
     rfb::Engine& e = *ctx->engine;
     const rfb::Config& c = e.cfg();
     const size_t nq = c.num_queries, nc = c.num_classes;
@@ -160,7 +178,13 @@ rfdetr_status fetch_outputs(rfdetr_context* ctx, int batch, float* logits, float
         if (RFB_CUDA_FAIL(cudaMemcpyAsync(masks, e.masks(), (size_t)batch * nq * hw * 4, cudaMemcpyDeviceToHost, st)))
             return RFDETR_ERR_INFERENCE;
     }
-    return RFB_CUDA_FAIL(cudaStreamSynchronize(st)) ? RFDETR_ERR_INFERENCE : RFDETR_OK;
+    return RFDETR_OK;
+}
+
+rfdetr_status fetch_outputs(rfdetr_context* ctx, int batch, float* logits, float* boxes, float* masks) {
+    rfdetr_status s = enqueue_output_copies(ctx, batch, logits, boxes, masks);
+    if (s != RFDETR_OK) return s;
+    return RFB_CUDA_FAIL(cudaStreamSynchronize(ctx->engine->stream())) ? RFDETR_ERR_INFERENCE : RFDETR_OK;
 }
 
 // Run the forward for `batch` same-sized RGB images already packed at h_rgb.
@@ -369,6 +393,55 @@ extern "C" rfdetr_status rfdetr_b200_forward_rgb(rfdetr_context* ctx, const uint
     rfdetr_status s = forward_rgb_impl(ctx, rgb, batch, width, height);
     if (s != RFDETR_OK) return s;
     return fetch_outputs(ctx, batch, out_logits, out_boxes, out_masks);
+}
+
+extern "C" rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width,
+                                                int height, float* out_logits, float* out_boxes, float* out_masks) {
+    if (!ctx || !ctx->engine || !rgb || batch <= 0 || width <= 0 || height <= 0) return RFDETR_ERR_INVALID_ARG;
+    rfb::Engine& e = *ctx->engine;
+    if (RFB_CUDA_FAIL(cudaSetDevice(e.device()))) return RFDETR_ERR_INFERENCE;
+    rfdetr_status s = e.reserve(batch);  // synchronizes the engine stream before growing
+    if (s != RFDETR_OK) return s;
+    if (!ctx->copy_stream) {
+        if (RFB_CUDA_FAIL(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking)))
+            return RFDETR_ERR_INFERENCE;
+        for (int k = 0; k < 2; ++k)
+            if (RFB_CUDA_FAIL(cudaEventCreateWithFlags(&ctx->slot_ready[k], cudaEventDisableTiming)) ||
+                RFB_CUDA_FAIL(cudaEventCreateWithFlags(&ctx->slot_free[k], cudaEventDisableTiming)))
+                return RFDETR_ERR_INFERENCE;
+    }
+    const int k = ctx->next_slot;
+    ctx->next_slot ^= 1;
+    const size_t bytes = (size_t)batch * width * height * 3;
+    if (bytes > ctx->slot_cap[k]) {
+        // the slot's last reader must be done before it is replaced
+        if (RFB_CUDA_FAIL(cudaEventSynchronize(ctx->slot_free[k]))) return RFDETR_ERR_INFERENCE;
+        if (ctx->d_slot[k]) cudaFree(ctx->d_slot[k]);
+        ctx->d_slot[k] = nullptr;
+        ctx->slot_cap[k] = 0;
+        if (RFB_CUDA_FAIL(cudaMalloc(&ctx->d_slot[k], bytes))) return RFDETR_ERR_OUT_OF_MEMORY;
+        ctx->slot_cap[k] = bytes;
+    }
+    // upload behind the slot's previous reader, the forward behind the upload
+    if (RFB_CUDA_FAIL(cudaStreamWaitEvent(ctx->copy_stream, ctx->slot_free[k], 0)) ||
+        RFB_CUDA_FAIL(cudaMemcpyAsync(ctx->d_slot[k], rgb, bytes, cudaMemcpyHostToDevice, ctx->copy_stream)) ||
+        RFB_CUDA_FAIL(cudaEventRecord(ctx->slot_ready[k], ctx->copy_stream)) ||
+        RFB_CUDA_FAIL(cudaStreamWaitEvent(e.stream(), ctx->slot_ready[k], 0)))
+        return RFDETR_ERR_INFERENCE;
+    s = e.enqueue(batch, ctx->d_slot[k], width, height);
+    if (s != RFDETR_OK) return s;
+    if (RFB_CUDA_FAIL(cudaEventRecord(ctx->slot_free[k], e.stream()))) return RFDETR_ERR_INFERENCE;
+    return enqueue_output_copies(ctx, batch, out_logits, out_boxes, out_masks);
+}
+
+extern "C" rfdetr_status rfdetr_b200_wait(rfdetr_context* ctx) {
+    if (!ctx || !ctx->engine) return RFDETR_ERR_INVALID_ARG;
+    if (ctx->copy_stream) {
+        if (RFB_CUDA_FAIL(cudaSetDevice(ctx->engine->device())) ||
+            RFB_CUDA_FAIL(cudaStreamSynchronize(ctx->copy_stream)))
+            return RFDETR_ERR_INFERENCE;
+    }
+    return ctx->engine->finish();
 }
 
 extern "C" rfdetr_status rfdetr_b200_forward_planar(rfdetr_context* ctx, const float* planar, int batch,

@@ -541,6 +541,43 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         }
                     }
                 }
+            } else if (EPI == EPI_PATCH && p.patch_vec) {
+                // window remap + position add: each 32-column chunk goes through the warp's staging box,
+                // then 8 lanes write one 128-byte row (4 rows per instruction), so the remapped stores
+                // and the position loads are coalesced
+                for (int c0 = col_begin; c0 < col_end; c0 += 32) {
+                    tmem_ld32(tbase + c0, raw);
+                    const int n0 = nt * BN + c0;
+                    const float bl = (p.bias && n0 + lane < p.N) ? p.bias[n0 + lane] : 0.f;
+                    tmem_wait_ld();
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        st_shared_v4(swz(wbuf, lane, j),
+                                     __float_as_uint(__uint_as_float(raw[4 * j]) + bcast(bl, 4 * j)),
+                                     __float_as_uint(__uint_as_float(raw[4 * j + 1]) + bcast(bl, 4 * j + 1)),
+                                     __float_as_uint(__uint_as_float(raw[4 * j + 2]) + bcast(bl, 4 * j + 2)),
+                                     __float_as_uint(__uint_as_float(raw[4 * j + 3]) + bcast(bl, 4 * j + 3)));
+                    __syncwarp();
+                    const int ch = lane & 7;
+                    const int n = n0 + 4 * ch;
+#pragma unroll 2
+                    for (int it = 0; it < 8; ++it) {
+                        const int r = it * 4 + (lane >> 3);
+                        const int mr = mt * BM + quad * 32 + r;
+                        if (mr < p.M && n < p.N) {
+                            float4 x = ld_shared_v4f(swz(wbuf, r, ch));
+                            const int img = mr / p.patch_rows;
+                            const int rr = mr - img * p.patch_rows;
+                            const int win = rr / p.patch_tp;
+                            const int tok = win * p.patch_t + 1 + (rr - win * p.patch_tp);
+                            const float4 ps = __ldg(reinterpret_cast<const float4*>(p.posw + (size_t)tok * p.N + n));
+                            x.x += ps.x; x.y += ps.y; x.z += ps.z; x.w += ps.w;
+                            *reinterpret_cast<float4*>(p.out32 + ((size_t)img * p.patch_ntok + tok) * p.ld32 + n) = x;
+                        }
+                    }
+                    __syncwarp();
+                }
             } else {
                 // direct stores (PATCH remap, or outputs a TMA map cannot describe)
                 for (int c0 = col_begin; c0 < col_end; c0 += 32) {
@@ -699,6 +736,8 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     if (tma && a.out16) tma = make_out_map(&to16, a.out16, true, a.N, a.M, a.batches, a.ld16, a.out_batch_stride);
     if (tma && a.out32) tma = make_out_map(&to32, a.out32, false, a.N, a.M, a.batches, a.ld32, a.out_batch_stride);
     a.tma_out = tma ? 1 : 0;
+    a.patch_vec = (EPI == EPI_PATCH && a.N % 4 == 0 && a.ld32 % 4 == 0 && !((uintptr_t)a.out32 & 15) &&
+                   !((uintptr_t)a.posw & 15)) ? 1 : 0;
     constexpr int TM = CTA2 ? 2 * BM : BM;
     const int m_tiles = CONV ? ((a.conv_h + a.conv_r - 1) / a.conv_r) * (a.M / (a.conv_h * a.conv_w))
                              : (a.M + TM - 1) / TM;

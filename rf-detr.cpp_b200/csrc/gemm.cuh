@@ -66,6 +66,7 @@ struct GemmArgs {
     int conv_r = 0;        // set by the launcher: image rows per 128-row tile
     int* err = nullptr;    // device error word
     int tma_out = 0;       // set by the launcher: outputs written through TMA stores
+    int patch_vec = 0;     // set by the launcher: EPI_PATCH rows written as 16-byte chunks
 };
 
 // Launch on `stream`.  Picks the tile width from N (and requires BN == N for

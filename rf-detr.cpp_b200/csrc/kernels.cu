@@ -104,13 +104,13 @@ __global__ void __launch_bounds__(256) k_patch_from_rgb(const uint8_t* __restric
     }
     const int G = S / p, ws = G / nw, Tp = ws * ws;
     const int chunks = Kpad / 8;
-    const size_t rows = (size_t)B * nw * nw * Tp;
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int rows = B * nw * nw * Tp;  // 32-bit indices (the host checks rows * chunks < 2^31)
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= rows * chunks) return;
-    const size_t row = i / chunks;
-    const int k0 = (int)(i - row * chunks) * 8;
-    const int b = (int)(row / ((size_t)nw * nw * Tp));
-    const int rr = (int)(row - (size_t)b * nw * nw * Tp);
+    const int row = i / chunks;
+    const int k0 = (i - row * chunks) * 8;
+    const int b = row / (nw * nw * Tp);
+    const int rr = row - b * nw * nw * Tp;
     const int win = rr / Tp, t = rr - win * Tp;
     const int gy = (win / nw) * ws + t / ws, gx = (win % nw) * ws + t % ws;
     const uint8_t* img = rgb + (size_t)b * h * w * 3;
@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(256) k_patch_from_rgb(const uint8_t* __restric
         __half2 hv = __floats2half2_rn(v2[0], v2[1]);
         out[e >> 1] = *reinterpret_cast<uint32_t*>(&hv);
     }
-    *reinterpret_cast<uint4*>(A + row * Kpad + k0) = make_uint4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<uint4*>(A + (size_t)row * Kpad + k0) = make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 __global__ void k_cls_rows(float* __restrict__ x, const float* __restrict__ clsrow, int B, int NW, int T, int D) {
@@ -647,6 +647,7 @@ cudaError_t patch_from_rgb(const uint8_t* rgb, int B, int w, int h, int S, int p
     const size_t rows = (size_t)B * nw * nw * Tp;
     if (Kpad % 8 || Kpad < 3 * p * p || ((uintptr_t)A & 15)) return cudaErrorInvalidValue;  // 16-byte stores
     const size_t n = rows * (Kpad / 8);
+    if (n >= (1ull << 31)) return cudaErrorInvalidValue;
     k_patch_from_rgb<<<cdiv(n, 256), 256, 0, st>>>(rgb, B, w, h, S, p, nw, Kpad, mean3[0], mean3[1], mean3[2],
                                                    std3[0], std3[1], std3[2], A);
     return cudaGetLastError();

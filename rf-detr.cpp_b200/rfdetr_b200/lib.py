@@ -100,6 +100,9 @@ SIGNATURES = {
     "rfdetr_b200_forward_planar": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "rfdetr_b200_enqueue_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]),
     "rfdetr_b200_sync": (C.c_int, [C.c_void_p]),
+    "rfdetr_b200_submit_rgb": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                         C.c_void_p, C.c_void_p]),
+    "rfdetr_b200_wait": (C.c_int, [C.c_void_p]),
     "rfdetr_b200_device_outputs": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                              C.POINTER(C.c_void_p)]),
     "rfdetr_b200_detect_batch": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.c_size_t, C.POINTER(DetectParams),
@@ -224,6 +227,17 @@ class Engine:
         check(lib().rfdetr_b200_forward_rgb(self._ctx, _ptr(rgb), B, W, H, _ptr(lg), _ptr(bx), _ptr(mk)),
               "forward_rgb")
         return lg, bx, mk
+
+    def submit_rgb(self, rgb: np.ndarray, logits: np.ndarray, boxes: np.ndarray, masks=None):
+        """Pipelined forward from host images into caller-owned output arrays
+        (kept alive and untouched until wait()); returns at once."""
+        B, H, W, _ = rgb.shape
+        assert rgb.flags.c_contiguous and rgb.dtype == np.uint8
+        check(lib().rfdetr_b200_submit_rgb(self._ctx, _ptr(rgb), B, W, H, _ptr(logits), _ptr(boxes),
+                                           _ptr(masks) if masks is not None else None), "submit_rgb")
+
+    def wait(self):
+        check(lib().rfdetr_b200_wait(self._ctx), "wait")
 
     def trace(self, name: str, batch: int, size_hint: int = 1 << 26) -> np.ndarray:
         out = np.zeros(size_hint, np.float32)

@@ -156,6 +156,34 @@ def test_graph_replay_matches_direct_launches(make_model, monkeypatch):
     assert np.array_equal(lb_direct, lb_direct2)
 
 
+def test_pipelined_submissions_match_forward_rgb(make_model):
+    """rfdetr_b200_submit_rgb / rfdetr_b200_wait: several batches in flight
+    (uploads on a copy stream into two alternating device slots, forwards and
+    output copies on the engine stream) give, batch for batch, the outputs of
+    the synchronous rfdetr_b200_forward_rgb; a larger batch and another image
+    size in the middle of the stream regrow the slots."""
+    import torch
+    from rfdetr_b200 import lib
+
+    path = make_model("tiny", "f16", 0)
+    S = 128
+    eng = lib.Engine(path, max_batch=2)
+    batches = [_images(S, 2, 31), _images(S, 2, 32), _images(S, 1, 33), _images(S + 40, 3, 34), _images(S, 2, 35)]
+    want = [eng.forward_rgb(x)[:2] for x in batches]
+    pinned = [torch.from_numpy(x).pin_memory() for x in batches]
+    outs = []
+    for x in pinned:
+        B = x.shape[0]
+        lg = torch.empty((B, eng.nq, eng.nc), dtype=torch.float32).pin_memory()
+        bx = torch.empty((B, eng.nq, 4), dtype=torch.float32).pin_memory()
+        eng.submit_rgb(x.numpy(), lg.numpy(), bx.numpy())
+        outs.append((lg, bx))
+    eng.wait()
+    for (lg, bx), (wl, wb) in zip(outs, want):
+        assert np.array_equal(lg.numpy(), wl) and np.array_equal(bx.numpy(), wb)
+    eng.close()
+
+
 # Every configuration the benchmark description names, at its real model size
 # (batch 2: the oracle checks both images; the full batches run through the
 # same kernels, only more rows).
