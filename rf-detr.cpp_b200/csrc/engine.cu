@@ -633,8 +633,8 @@ rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int 
     // in f16 from the same tile.  That tile is 384 columns wide, so it has a
     // single TMEM accumulator and its epilogue does not overlap the next
     // tile's mainloop; measured on B200 (RF-DETR Base, batch 32) the separate
-    // TMA reduce-add GEMM + LayerNorm kernel is faster (7.82 vs 8.32 ms per
-    // forward), so it is the default.
+    // TMA reduce-add GEMM + LayerNorm kernel is faster (6.73 vs 7.28 ms per
+    // forward; proj + norm2 37.9 + 23.7 µs vs 83.5 µs fused), so it is the default.
     const float scale = 1.0f / std::sqrt((float)(D / H_));
     const bool fuse_ln = RFB_FUSE_LN && (D == 128 || D == 256 || D == 384);
     const bool use_mlp = RFB_FUSED_MLP && mlp_supported(D, F_);
