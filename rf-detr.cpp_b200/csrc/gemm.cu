@@ -852,7 +852,8 @@ cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
         if (a.N != 128 && a.N != 256 && a.N != 384) return cudaErrorInvalidValue;
         if (!a.ln_g || !a.ln_b) return cudaErrorInvalidValue;
         bn = a.N;
-    } else if (a.N == 384 && a.epi == EPI_RESID && a.act == ACT_NONE && a.K >= 768 && wide_resid()) {
+    } else if (a.N == 384 && a.epi == EPI_RESID && a.act == ACT_NONE && a.K >= 768 && wide_resid() &&
+               (long long)((a.M + BM - 1) / BM) * a.batches >= g_num_sms) {
         bn = 384;  // one full-row tile: A crosses from L2 once per row block instead of twice
     } else if (a.N % 256 == 0) {
         bn = 256;
@@ -864,6 +865,14 @@ cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
         bn = 64;
     }
     if (a.epi != EPI_LN) {
+        // few row blocks (small batches): narrower tiles until the grid covers every SM, so a
+        // batch-1 forward does not run its GEMMs on a tenth of the GPU
+        const long long m_tiles = (long long)((a.M + BM - 1) / BM) * a.batches;
+        auto tiles = [&](int w) { return m_tiles * ((a.N + w - 1) / w); };
+        for (const int w : {128, 64}) {
+            if (tiles(bn) >= g_num_sms || w >= bn) continue;
+            bn = w;
+        }
         // tuning override: RFDETR_GEMM_BN = 128 / 192 / 256 where it divides N
         const char* env = std::getenv("RFDETR_GEMM_BN");
         const int f = env ? std::atoi(env) : 0;
