@@ -25,6 +25,13 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// x / d for 0 <= x < 2^21 through a float reciprocal: (x + 1/2) * (1/d) lies at
+// least 1/(2d) from the next integer, and the float error of that product is
+// below (x/d) * 2^-22 < 1/(2d) in that range, so truncation gives the quotient.
+__device__ __forceinline__ int div_small(int x, float inv_d) {
+    return __float2int_rz(__fmul_rn((float)x + 0.5f, inv_d));
+}
+
 // ---- preprocess: src/image_io.cpp:207-248 ----------------------------------
 __global__ void k_preprocess(const uint8_t* __restrict__ rgb, int B, int w, int h, int S, float m0, float m1,
                              float m2, float s0, float s1, float s2, float* __restrict__ out) {
@@ -83,12 +90,12 @@ __global__ void k_patch_im2col(const float* __restrict__ img, int B, int S, int 
 // Preprocess (src/image_io.cpp:207-248) fused into the patch im2col: each
 // im2col element is one normalized model-resolution pixel, sampled straight
 // from the uint8 source with the same double-precision source coordinates.
-// One thread per 8 consecutive im2col elements of a row (one 16-byte store):
-// element k of a row is (channel, kernel row, kernel column) =
-// (k / p^2, k / p mod p, k mod p); elements past 3 p^2 are the zero K padding.
-// Without resizing, every element is (u / 255 - mean_c) / std_c of a source
-// byte u: a per-block table of those 768 floats (the same float expression)
-// replaces the two divisions per element.
+// One warp per im2col row (grid-strided); lane l writes the 16-byte chunks
+// l, l + 32, l + 64 (8 consecutive elements each).  Element k of a row is
+// (channel, kernel row, kernel column) = (k / p^2, k / p mod p, k mod p);
+// elements past 3 p^2 are the zero K padding.  Without resizing, every element
+// is (u / 255 - mean_c) / std_c of a source byte u: a per-block table of those
+// 768 floats (the same float expression) replaces the two divisions.
 __global__ void __launch_bounds__(256) k_patch_from_rgb(const uint8_t* __restrict__ rgb, int B, int w, int h, int S,
                                                         int p, int nw, int Kpad, float m0, float m1, float m2,
                                                         float s0, float s1, float s2, __half* __restrict__ A) {
@@ -102,67 +109,74 @@ __global__ void __launch_bounds__(256) k_patch_from_rgb(const uint8_t* __restric
         }
         __syncthreads();
     }
-    const int G = S / p, ws = G / nw, Tp = ws * ws;
-    const int chunks = Kpad / 8;
-    const int rows = B * nw * nw * Tp;  // 32-bit indices (the host checks rows * chunks < 2^31)
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= rows * chunks) return;
-    const int row = i / chunks;
-    const int k0 = (i - row * chunks) * 8;
-    const int b = row / (nw * nw * Tp);
-    const int rr = row - b * nw * nw * Tp;
-    const int win = rr / Tp, t = rr - win * Tp;
-    const int gy = (win / nw) * ws + t / ws, gx = (win % nw) * ws + t % ws;
-    const uint8_t* img = rgb + (size_t)b * h * w * 3;
-    const int kreal = 3 * p * p;
-    int c = k0 / (p * p);
-    int ky = (k0 - c * p * p) / p;
-    int kx = k0 - c * p * p - ky * p;
+    const int G = S / p, ws = G / nw, Tp = ws * ws, NT = nw * nw * Tp;
+    const int chunks = Kpad / 8, kreal = 3 * p * p;
+    const int rows = B * NT;  // < 2^21 (checked by the host)
+    const float inv_nt = 1.0f / (float)NT, inv_tp = 1.0f / (float)Tp, inv_ws = 1.0f / (float)ws;
+    const float inv_nw = 1.0f / (float)nw, inv_pp = 1.0f / (float)(p * p), inv_p = 1.0f / (float)p;
     const double scx = (double)w / (double)S, scy = (double)h / (double)S;
-    uint32_t out[4];
+    const int lane = threadIdx.x & 31;
+    const int wstride = gridDim.x * (blockDim.x >> 5);
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += wstride) {
+        const int b = div_small(row, inv_nt);
+        const int rr = row - b * NT;
+        const int win = div_small(rr, inv_tp), t = rr - win * Tp;
+        const int wy = div_small(win, inv_nw), ty = div_small(t, inv_ws);
+        const int gy = wy * ws + ty, gx = (win - wy * nw) * ws + (t - ty * ws);
+        const uint8_t* img = rgb + (size_t)b * h * w * 3;
+        __half* arow = A + (size_t)row * Kpad;
+        for (int ch = lane; ch < chunks; ch += 32) {
+            const int k0 = ch * 8;
+            int c = div_small(k0, inv_pp);
+            int ky = div_small(k0 - c * p * p, inv_p);
+            int kx = k0 - c * p * p - ky * p;
+            uint32_t out[4];
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-        float v2[2];
+            for (int e = 0; e < 8; e += 2) {
+                float v2[2];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            float v = 0.f;
-            if (k0 + e + u < kreal) {
-                const int yy = gy * p + ky, xx = gx * p + kx;
-                if (identity) {
-                    // identity resize: source coordinate == destination, interpolation weights 0
-                    v = lut[(c << 8) + img[((size_t)yy * w + xx) * 3 + c]];
-                } else {
-                    const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2), sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
-                    const double fy = ((double)yy + 0.5) * scy - 0.5;
-                    const int y0r = (int)floor(fy);
-                    const int y0 = min(max(y0r, 0), h - 1), y1 = min(max(y0r + 1, 0), h - 1);
-                    const float wy = (float)(fy - (double)y0r);
-                    const double fx = ((double)xx + 0.5) * scx - 0.5;
-                    const int x0r = (int)floor(fx);
-                    const int x0 = min(max(x0r, 0), w - 1), x1 = min(max(x0r + 1, 0), w - 1);
-                    const float wx = (float)(fx - (double)x0r);
-                    const float p00 = (float)img[((size_t)y0 * w + x0) * 3 + c];
-                    const float p01 = (float)img[((size_t)y0 * w + x1) * 3 + c];
-                    const float p10 = (float)img[((size_t)y1 * w + x0) * 3 + c];
-                    const float p11 = (float)img[((size_t)y1 * w + x1) * 3 + c];
-                    const float top = p00 + (p01 - p00) * wx;
-                    const float bot = p10 + (p11 - p10) * wx;
-                    v = ((top + (bot - top) * wy) / 255.0f - mean) / sd;
+                for (int u = 0; u < 2; ++u) {
+                    float v = 0.f;
+                    if (k0 + e + u < kreal) {
+                        const int yy = gy * p + ky, xx = gx * p + kx;
+                        if (identity) {
+                            // identity resize: source coordinate == destination, interpolation weights 0
+                            v = lut[(c << 8) + img[((size_t)yy * w + xx) * 3 + c]];
+                        } else {
+                            const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
+                            const float sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+                            const double fy = ((double)yy + 0.5) * scy - 0.5;
+                            const int y0r = (int)floor(fy);
+                            const int y0 = min(max(y0r, 0), h - 1), y1 = min(max(y0r + 1, 0), h - 1);
+                            const float wy_ = (float)(fy - (double)y0r);
+                            const double fx = ((double)xx + 0.5) * scx - 0.5;
+                            const int x0r = (int)floor(fx);
+                            const int x0 = min(max(x0r, 0), w - 1), x1 = min(max(x0r + 1, 0), w - 1);
+                            const float wx = (float)(fx - (double)x0r);
+                            const float p00 = (float)img[((size_t)y0 * w + x0) * 3 + c];
+                            const float p01 = (float)img[((size_t)y0 * w + x1) * 3 + c];
+                            const float p10 = (float)img[((size_t)y1 * w + x0) * 3 + c];
+                            const float p11 = (float)img[((size_t)y1 * w + x1) * 3 + c];
+                            const float top = p00 + (p01 - p00) * wx;
+                            const float bot = p10 + (p11 - p10) * wx;
+                            v = ((top + (bot - top) * wy_) / 255.0f - mean) / sd;
+                        }
+                    }
+                    v2[u] = v;
+                    if (++kx == p) {
+                        kx = 0;
+                        if (++ky == p) {
+                            ky = 0;
+                            ++c;
+                        }
+                    }
                 }
+                __half2 hv = __floats2half2_rn(v2[0], v2[1]);
+                out[e >> 1] = *reinterpret_cast<uint32_t*>(&hv);
             }
-            v2[u] = v;
-            if (++kx == p) {
-                kx = 0;
-                if (++ky == p) {
-                    ky = 0;
-                    ++c;
-                }
-            }
+            *reinterpret_cast<uint4*>(arow + k0) = make_uint4(out[0], out[1], out[2], out[3]);
         }
-        __half2 hv = __floats2half2_rn(v2[0], v2[1]);
-        out[e >> 1] = *reinterpret_cast<uint32_t*>(&hv);
     }
-    *reinterpret_cast<uint4*>(A + (size_t)row * Kpad + k0) = make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 __global__ void k_cls_rows(float* __restrict__ x, const float* __restrict__ clsrow, int B, int NW, int T, int D) {
@@ -219,12 +233,14 @@ __global__ void k_layernorm(const float* x, int rows, int D, const float* __rest
 // first in each window) and written at column col0 of an f16 row of pitch ld.
 struct TapMap {
     int G = 0, nw = 1, ld = 0, col0 = 0;
+    float inv_gg = 0.f, inv_g = 0.f, inv_ws = 0.f;  // 1 / G^2, 1 / G, 1 / (G / nw)
     __device__ __forceinline__ size_t src_row(int r) const {
-        const int b = r / (G * G), pix = r - b * G * G;
-        const int gy = pix / G, gx = pix - gy * G;
-        const int ws = G / nw, T = ws * ws + 1;
-        const int win = (gy / ws) * nw + gx / ws;
-        return (size_t)b * nw * nw * T + win * T + 1 + (gy % ws) * ws + gx % ws;
+        const int GG = G * G, ws = G / nw, T = ws * ws + 1;
+        const int b = div_small(r, inv_gg), pix = r - b * GG;
+        const int gy = div_small(pix, inv_g), gx = pix - gy * G;
+        const int wy = div_small(gy, inv_ws), wx = div_small(gx, inv_ws);
+        const int win = wy * nw + wx;
+        return (size_t)b * nw * nw * T + win * T + 1 + (gy - wy * ws) * ws + (gx - wx * ws);
     }
 };
 
@@ -646,9 +662,9 @@ cudaError_t patch_from_rgb(const uint8_t* rgb, int B, int w, int h, int S, int p
     const int G = S / p, Tp = (G / nw) * (G / nw);
     const size_t rows = (size_t)B * nw * nw * Tp;
     if (Kpad % 8 || Kpad < 3 * p * p || ((uintptr_t)A & 15)) return cudaErrorInvalidValue;  // 16-byte stores
-    const size_t n = rows * (Kpad / 8);
-    if (n >= (1ull << 31)) return cudaErrorInvalidValue;
-    k_patch_from_rgb<<<cdiv(n, 256), 256, 0, st>>>(rgb, B, w, h, S, p, nw, Kpad, mean3[0], mean3[1], mean3[2],
+    if (rows >= (1u << 21)) return cudaErrorInvalidValue;
+    const unsigned blocks = cdiv(rows, 8) < 148u * 8u ? cdiv(rows, 8) : 148u * 8u;  // warp per row, grid-strided
+    k_patch_from_rgb<<<blocks, 256, 0, st>>>(rgb, B, w, h, S, p, nw, Kpad, mean3[0], mean3[1], mean3[2],
                                                    std3[0], std3[1], std3[2], A);
     return cudaGetLastError();
 }
@@ -677,11 +693,14 @@ cudaError_t backbone_tap(const float* x, int B, int G, int nw, int D, const floa
                          int ld, int col0, cudaStream_t st) {
     if (D > 384) return cudaErrorInvalidValue;
     const int rows = B * G * G;
-    if ((D == 384 || D == 256) && ld % 4 == 0 && col0 % 4 == 0 && !(((uintptr_t)x | (uintptr_t)taps) & 15) &&
+    if ((D == 384 || D == 256) && rows < (1 << 21) && ld % 4 == 0 && col0 % 4 == 0 && !(((uintptr_t)x | (uintptr_t)taps) & 15) &&
         !(((uintptr_t)g | (uintptr_t)b) & 15)) {
         // vectorised, grid-strided LayerNorm over the gathered rows (8-byte f16 stores)
         TapMap tm;
         tm.G = G; tm.nw = nw; tm.ld = ld; tm.col0 = col0;
+        tm.inv_gg = 1.0f / (float)(G * G);
+        tm.inv_g = 1.0f / (float)G;
+        tm.inv_ws = 1.0f / (float)(G / nw);
         const unsigned blocks = cdiv(rows, 8) < (unsigned)(148 * 6) ? cdiv(rows, 8) : (unsigned)(148 * 6);
         if (D == 384) k_layernorm_v4<3, true><<<blocks, 256, 0, st>>>(x, rows, g, b, 1e-6f, nullptr, taps, tm);
         else k_layernorm_v4<2, true><<<blocks, 256, 0, st>>>(x, rows, g, b, 1e-6f, nullptr, taps, tm);
