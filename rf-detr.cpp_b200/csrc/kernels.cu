@@ -418,16 +418,43 @@ __global__ void __launch_bounds__(1024) k_topk(const float* __restrict__ cls, in
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     int P = 1;
     while (P < N) P <<= 1;
-    for (int t = warp; t < P; t += nwarps) {
-        unsigned long long key = ~0ull;
-        if (t < N) {
-            const float* r = cls + ((size_t)b * N + t) * NC;
-            float m = -INFINITY;
-            for (int c = lane; c < NC; c += 32) m = fmaxf(m, r[c]);
-            m = warp_max(m);
-            key = ((unsigned long long)(~float_order(m)) << 32) | (unsigned)t;
+    if (NC <= 96) {
+        // 8 tokens per warp at a time, every class load issued before the reductions: the
+        // row maxima are bound by load latency, not bandwidth
+        constexpr int U = 8;
+        for (int t0 = warp * U; t0 < P; t0 += nwarps * U) {
+            float m[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int t = t0 + u;
+                m[u] = -INFINITY;
+                if (t < N) {
+                    const float* r = cls + ((size_t)b * N + t) * NC;
+#pragma unroll
+                    for (int j = 0; j < 3; ++j)
+                        if (lane + 32 * j < NC) m[u] = fmaxf(m[u], r[lane + 32 * j]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int t = t0 + u;
+                const float mu = warp_max(m[u]);
+                if (lane == 0 && t < P)
+                    keys[t] = t < N ? ((unsigned long long)(~float_order(mu)) << 32) | (unsigned)t : ~0ull;
+            }
         }
-        if (lane == 0) keys[t] = key;
+    } else {
+        for (int t = warp; t < P; t += nwarps) {
+            unsigned long long key = ~0ull;
+            if (t < N) {
+                const float* r = cls + ((size_t)b * N + t) * NC;
+                float m = -INFINITY;
+                for (int c = lane; c < NC; c += 32) m = fmaxf(m, r[c]);
+                m = warp_max(m);
+                key = ((unsigned long long)(~float_order(m)) << 32) | (unsigned)t;
+            }
+            if (lane == 0) keys[t] = key;
+        }
     }
     __syncthreads();
     // bitonic sort ascending (smaller key = higher score, then lower index)
