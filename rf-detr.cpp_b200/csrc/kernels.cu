@@ -458,6 +458,66 @@ __global__ void __launch_bounds__(1024) k_topk(const float* __restrict__ cls, in
     }
     __syncthreads();
     // bitonic sort ascending (smaller key = higher score, then lower index)
+    if (P >= 64 && P <= 2 * (int)blockDim.x) {
+        // thread t < P/2 owns keys 2t and 2t+1: the stages whose partner distance j is at most 32
+        // run in registers (j = 1 inside the thread, 2..32 by warp shuffles, partner thread t ^ j/2);
+        // only the wider ones go through shared memory
+        const int t = threadIdx.x;
+        const bool act = t < P / 2;
+        unsigned long long k0 = act ? keys[2 * t] : 0ull, k1 = act ? keys[2 * t + 1] : 0ull;
+        for (int k = 2; k <= P; k <<= 1) {
+            int j = k >> 1;
+            if (j >= 64) {
+                __syncthreads();
+                if (act) {
+                    keys[2 * t] = k0;
+                    keys[2 * t + 1] = k1;
+                }
+                __syncthreads();
+                for (; j >= 64; j >>= 1) {
+                    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                        const int ixj = i ^ j;
+                        if (ixj > i) {
+                            const unsigned long long a = keys[i], c = keys[ixj];
+                            const bool up = (i & k) == 0;
+                            if ((a > c) == up) {
+                                keys[i] = c;
+                                keys[ixj] = a;
+                            }
+                        }
+                    }
+                    __syncthreads();
+                }
+                if (act) {
+                    k0 = keys[2 * t];
+                    k1 = keys[2 * t + 1];
+                }
+            }
+            if (act) {
+                const bool up = ((2 * t) & k) == 0;  // the same for both keys (k >= 2)
+                for (; j >= 2; j >>= 1) {
+                    const int d = j >> 1;                       // partner thread t ^ d, same slot
+                    const bool lower = ((2 * t) & j) == 0;      // this thread holds the lower index
+                    const unsigned long long p0 = __shfl_xor_sync(0xffffffffu, k0, d);
+                    const unsigned long long p1 = __shfl_xor_sync(0xffffffffu, k1, d);
+                    const bool keep_min = lower == up;
+                    k0 = keep_min ? (k0 < p0 ? k0 : p0) : (k0 > p0 ? k0 : p0);
+                    k1 = keep_min ? (k1 < p1 ? k1 : p1) : (k1 > p1 ? k1 : p1);
+                }
+                if ((k0 > k1) == up) {
+                    const unsigned long long tmp = k0;
+                    k0 = k1;
+                    k1 = tmp;
+                }
+            }
+        }
+        __syncthreads();
+        if (act) {
+            keys[2 * t] = k0;
+            keys[2 * t + 1] = k1;
+        }
+        __syncthreads();
+    } else {
     for (int k = 2; k <= P; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
             for (int i = threadIdx.x; i < P; i += blockDim.x) {
@@ -473,6 +533,7 @@ __global__ void __launch_bounds__(1024) k_topk(const float* __restrict__ cls, in
             }
             __syncthreads();
         }
+    }
     }
     for (int q = threadIdx.x; q < K; q += blockDim.x) idx[(size_t)b * K + q] = (int32_t)(keys[q] & 0xffffffffu);
 }
