@@ -49,13 +49,17 @@ struct Cfg {
     static constexpr int B_ROWS = CTA2 ? BN / 2 : BN;
     static constexpr int NEPI = 8;  // epilogue warps: two per TMEM lane quadrant
     static constexpr int THREADS = 64 + 32 * NEPI;
-    static constexpr int STAGES = CTA2 ? (BN >= 192 ? 6 : 8) : (BN > 256 ? 3 : (BN >= 192 ? 4 : (BN == 128 ? 6 : 8)));
-    static_assert(!CTA2 || BN <= 256, "pair tiles: one MMA of N <= 256 over both CTAs' B halves");
+    static constexpr int STAGES =
+        CTA2 ? (BN > 256 ? 4 : (BN >= 192 ? 6 : 8)) : (BN > 256 ? 3 : (BN >= 192 ? 4 : (BN == 128 ? 6 : 8)));
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = NACC == 1 ? 512 : (BN == 192 ? 512 : 2 * BN);  // power of two
-    static constexpr int NSPLIT = B_ROWS > 256 ? 2 : 1;  // B tile in NSPLIT TMA boxes / MMAs of N <= 256
+    // the tile's columns as NSPLIT slabs of one MMA each (N <= 256); a CTA loads HSLAB rows of B per
+    // slab: the whole slab, or with CTA2 its half of it (the pair MMA reads both CTAs' halves)
+    static constexpr int NSPLIT = BN > 256 ? 2 : 1;
+    static constexpr int SLAB = BN / NSPLIT;
+    static constexpr int HSLAB = B_ROWS / NSPLIT;
     static constexpr int OUT_STAGE = NEPI * 4096;  // per epilogue warp: one 32-row x 128-byte box
     static constexpr int RED_BYTES = EPI == EPI_LN ? 1024 : 0;  // LN: per-row partial sums of 2 warps
     static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*align*/ + 256 /*barriers*/ + RED_BYTES;
@@ -143,7 +147,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 const int r = tile - b * tiles_per_batch;
                 const int mt = r / n_tiles, nt = r - mt * n_tiles;
                 const int arow = b * p.a_batch_rows + mt * TM + (int)rank * BM;
-                const int brow = b * p.b_batch_rows + nt * BN + (int)rank * C::B_ROWS;
+                const int brow = b * p.b_batch_rows + nt * BN + (int)rank * C::HSLAB;  // + sp * SLAB
                 const int cimg = CONV ? mt / conv_tpi : 0;
                 const int cy0 = CONV ? (mt - cimg * conv_tpi) * p.conv_r : 0;
                 const int cch = CONV ? p.conv_c / BK : 1;  // 64-channel chunks per tap
@@ -153,7 +157,10 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);  // both halves
                         const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
                         tma_load_2d_peer_bar(&tmA, fb, sA + stage * C::A_BYTES, kb * BK, arow);
-                        tma_load_2d_peer_bar(&tmB, fb, sB + stage * C::B_BYTES, kb * BK, brow);
+#pragma unroll
+                        for (int sp = 0; sp < C::NSPLIT; ++sp)
+                            tma_load_2d_peer_bar(&tmB, fb, sB + stage * C::B_BYTES + sp * C::HSLAB * 128, kb * BK,
+                                                 brow + sp * C::SLAB);
                         PAIR_DBG(0 + rank);
                     } else if constexpr (CONV) {
                         // box (64 channels, conv_w pixels, conv_r rows) of the map shifted by the tap
@@ -168,8 +175,8 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     if constexpr (!CTA2) {
 #pragma unroll
                         for (int sp = 0; sp < C::NSPLIT; ++sp)
-                            tma_load_2d(&tmB, &full[stage], sB + stage * C::B_BYTES + sp * (BN / C::NSPLIT) * 128,
-                                        kb * BK, brow + sp * (BN / C::NSPLIT));
+                            tma_load_2d(&tmB, &full[stage], sB + stage * C::B_BYTES + sp * C::HSLAB * 128, kb * BK,
+                                        brow + sp * C::SLAB);
                     }
                     if (++stage == C::STAGES) {
                         stage = 0;
@@ -180,7 +187,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t IDESC = idesc_f16_f32(TM, BN / C::NSPLIT);
+            constexpr uint32_t IDESC = idesc_f16_f32(TM, C::SLAB);
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
@@ -198,15 +205,12 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
-                        if constexpr (CTA2) {
-                            umma_f16_pair(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32),
-                                          IDESC, (kb | kk) != 0);
-                        } else {
 #pragma unroll
-                            for (int sp = 0; sp < C::NSPLIT; ++sp)
-                                umma_f16(d_tmem + sp * (BN / C::NSPLIT), sw128_kmajor_desc(a0 + kk * 32),
-                                         sw128_kmajor_desc(b0 + sp * (BN / C::NSPLIT) * 128 + kk * 32), IDESC,
-                                         (kb | kk) != 0);
+                        for (int sp = 0; sp < C::NSPLIT; ++sp) {
+                            const uint64_t ad = sw128_kmajor_desc(a0 + kk * 32);
+                            const uint64_t bd = sw128_kmajor_desc(b0 + sp * C::HSLAB * 128 + kk * 32);
+                            if constexpr (CTA2) umma_f16_pair(d_tmem + sp * C::SLAB, ad, bd, IDESC, (kb | kk) != 0);
+                            else umma_f16(d_tmem + sp * C::SLAB, ad, bd, IDESC, (kb | kk) != 0);
                         }
                     }
                     if constexpr (CTA2) {
@@ -727,7 +731,7 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     } else if (!make_map(&ta, a.A, a.K, a_rows, a.lda, BM)) {
         return cudaErrorInvalidValue;
     }
-    if (!make_map(&tb, a.B, a.K, b_rows, a.ldb, C::B_ROWS / C::NSPLIT))
+    if (!make_map(&tb, a.B, a.K, b_rows, a.ldb, C::HSLAB))
         return cudaErrorInvalidValue;
     CUtensorMap to16, to32;
     std::memset(&to16, 0, sizeof(to16));
@@ -767,20 +771,21 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-// Two-SM tiles (256 x BN over a cluster of two CTAs) for the large plain
-// GEMMs: f16 / f32 / residual epilogues, BN 192 or 256, one batch, and at
-// least two 256-row tiles per SM pair.  RFDETR_GEMM_2SM=0 keeps single-SM
-// tiles, =1 takes two-SM tiles for every eligible shape.
+// Two-SM tiles (256 x BN over a cluster of two CTAs) for plain GEMMs: f16 /
+// f32 / residual epilogues, BN 192, 256 or 384 (residual only), one batch.
 bool use_pair(const GemmArgs& a, int bn) {
-    if (a.batches != 1 || (bn != 192 && bn != 256) || a.conv_src) return false;
+    if (a.batches != 1 || (bn != 192 && bn != 256 && bn != 384) || a.conv_src) return false;
     if (a.epi != EPI_F16 && a.epi != EPI_F32 && a.epi != EPI_RESID) return false;
-    // opt-in: RFDETR_GEMM_2SM=1 forces pair tiles, =auto uses them when
-    // there are at least two pair-tiles per pair of SMs; default off
+    // RFDETR_GEMM_2SM=0 never, =1 always, =auto whenever there are at least two pair-tiles per pair
+    // of SMs; by default only for the 384-wide residual tile (the MLP's long-K output GEMM), the
+    // one shape where pairs measured faster (Base batch 32: 72.3 -> 71.0 us; the K = 384 shapes
+    // are 5-15 % slower as pairs)
     const char* env = std::getenv("RFDETR_GEMM_2SM");
-    if (!env || env[0] == '0') return false;
-    if (env[0] == '1') return true;
+    if (env && env[0] == '0') return false;
+    if (env && env[0] == '1') return true;
     const long long tiles = (long long)((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + bn - 1) / bn);
-    return tiles >= (long long)g_num_sms;
+    if (env) return tiles >= (long long)g_num_sms;
+    return bn == 384 && tiles >= (long long)g_num_sms;
 }
 
 // Residual GEMMs of N = 384 and long K (the MLP's second linear) as one
@@ -794,6 +799,8 @@ template <int EPI, int ACT>
 cudaError_t dispatch_bn(const GemmArgs& a, int bn, cudaStream_t st) {
     if constexpr (EPI == EPI_F16 || EPI == EPI_F32 || EPI == EPI_RESID) {
         if (use_pair(a, bn)) {
+            if constexpr (EPI == EPI_RESID && ACT == ACT_NONE)
+                if (bn == 384) return launch<384, EPI, ACT, false, true>(a, st);
             if constexpr (ACT == ACT_NONE || ACT == ACT_GELU)
                 return bn == 256 ? launch<256, EPI, ACT, false, true>(a, st) : launch<192, EPI, ACT, false, true>(a, st);
         }

@@ -69,6 +69,45 @@ def test_gemm(M, N, K, epi, act):
         assert rel(out32, base.double() + scale.double() * ref) < 1e-4
 
 
+def _gemm_case(M, N, K, epi, act):
+    """One rfdetr_b200_op_gemm call on seeded data against float64 torch."""
+    torch.manual_seed(M * 7 + N + K)
+    dev = "cuda:0"
+    A = (torch.randn(M, K, device=dev)).half()
+    B = (torch.randn(N, K, device=dev) * 0.05).half()
+    bias = torch.randn(N, device=dev) * 0.1
+    scale = torch.rand(N, device=dev) + 0.5
+    ref = A.double() @ B.double().T + bias.double()
+    if act == 1:
+        ref = F.gelu(ref)
+    out16 = torch.zeros(M, N, dtype=torch.float16, device=dev) if epi == 0 else None
+    out32 = torch.randn(M, N, device=dev) if epi == 2 else None
+    base = out32.clone() if epi == 2 else None
+    rc = _lib().rfdetr_b200_op_gemm(_p(A), K, _p(B), K, M, N, K, epi, act, _p(bias), _p(scale) if epi == 2 else None,
+                                    None, None, 0.0, None, 0, _p(out32), N, _p(out16), N, _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    if epi == 0:
+        assert rel(out16, ref) < 2e-3
+    else:
+        assert rel(out32, base.double() + scale.double() * ref) < 1e-4
+
+
+@pytest.mark.parametrize("M,N,K,epi,act", [(300, 256, 256, 0, 0), (4097, 1536, 384, 0, 1), (1000, 1152, 384, 0, 0),
+                                           (4097, 384, 1536, 2, 0), (333, 384, 768, 2, 0), (2000, 256, 512, 2, 0)])
+def test_gemm_two_sm_tiles(M, N, K, epi, act, monkeypatch):
+    """Two-SM tiles (cta_group::2 over a cluster of two CTAs) forced on for every eligible shape: 192-,
+    256- and 384-wide tiles (the last as two N = 192 pair MMAs, each CTA holding half of each slab)."""
+    monkeypatch.setenv("RFDETR_GEMM_2SM", "1")
+    _gemm_case(M, N, K, epi, act)
+
+
+def test_gemm_large_residual_default_tiles():
+    """The MLP output GEMM at batch-32 scale (M = 40000, N = 384, K = 1536): by default it runs as
+    384-wide two-SM tiles."""
+    _gemm_case(40000, 384, 1536, 2, 0)
+
+
 @pytest.mark.parametrize("N", [128, 256, 384])
 @pytest.mark.parametrize("act,with_resid", [(0, True), (3, False)])
 @pytest.mark.parametrize("M", [777, 40000])
