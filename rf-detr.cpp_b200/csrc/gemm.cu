@@ -30,13 +30,6 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 
-#ifdef RFB_PAIR_DEBUG
-// progress counters of the two-SM path, read with rfdetr_b200_debug_pair (debug builds only)
-__device__ int g_pair_dbg[16];
-#define PAIR_DBG(i) atomicAdd(&g_pair_dbg[(i)], 1)
-#else
-#define PAIR_DBG(i) ((void)0)
-#endif
 
 template <int BN, int EPI, bool CTA2 = false>
 struct Cfg {
@@ -161,7 +154,6 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         for (int sp = 0; sp < C::NSPLIT; ++sp)
                             tma_load_2d_peer_bar(&tmB, fb, sB + stage * C::B_BYTES + sp * C::HSLAB * 128, kb * BK,
                                                  brow + sp * C::SLAB);
-                        PAIR_DBG(0 + rank);
                     } else if constexpr (CONV) {
                         // box (64 channels, conv_w pixels, conv_r rows) of the map shifted by the tap
                         const int tap = kb / cch, cc = kb - tap * cch;
@@ -199,7 +191,6 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait<CTA2>(&full[stage], phase, cta_abort, p.err)) goto done;
-                    if (CTA2) PAIR_DBG(2);
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
                     const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
@@ -216,7 +207,6 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     if constexpr (CTA2) {
                         umma_commit_pair(smem_u32(&empty[stage]));  // the stage is free in both CTAs
                         umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
-                        PAIR_DBG(3);
                     } else {
                         umma_commit(&empty[stage]);
                     }
@@ -228,7 +218,6 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 if constexpr (CTA2) {
                     umma_commit_pair(smem_u32(&tfull[acc]));  // both CTAs' accumulator halves are ready
                     umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
-                    PAIR_DBG(4);
                 } else {
                     umma_commit(&tfull[acc]);
                 }
@@ -266,7 +255,6 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 }
             }
             if (!__all_sync(0xffffffffu, mbar_wait<CTA2>(&tfull[acc], acc_phase, cta_abort, p.err))) goto done;
-            if (CTA2 && warp == 2 && lane == 0) PAIR_DBG(5 + rank);
             tc_fence_after();
             int m = mt * TM + (int)rank * BM + row_in_tile;
             const int m0w = mt * TM + (int)rank * BM + quad * 32;
@@ -819,19 +807,6 @@ cudaError_t dispatch_bn(const GemmArgs& a, int bn, cudaStream_t st) {
 
 void gemm_set_num_sms(int n) { g_num_sms = n > 0 ? n : 148; }
 
-#ifdef RFB_PAIR_DEBUG
-}  // namespace rfb
-extern "C" int rfdetr_b200_debug_pair(int* host16, int reset) {
-    cudaDeviceSynchronize();
-    cudaMemcpyFromSymbol(host16, rfb::g_pair_dbg, 16 * sizeof(int));
-    if (reset) {
-        int z[16] = {};
-        cudaMemcpyToSymbol(rfb::g_pair_dbg, z, sizeof(z));
-    }
-    return 0;
-}
-namespace rfb {
-#endif
 
 cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
     if (!load_encode()) return cudaErrorNotSupported;
