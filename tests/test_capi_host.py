@@ -190,6 +190,19 @@ def test_flat_capi_invalid_handles():
     assert L.rfdetr_capi_load(b"/nonexistent.gguf", 1, C.byref(h)) == -2 and h.value == 0
 
 
+def test_b200_entry_points_reject_null_handles():
+    """Host-side argument checks of the batch / pipelined entry points: a null
+    context or buffer is RFDETR_ERR_INVALID_ARG before any CUDA call."""
+    L = lib.lib()
+    buf = (C.c_uint8 * 12)()
+    out = (C.c_float * 4)()
+    assert L.rfdetr_b200_submit_rgb(None, buf, 1, 2, 2, out, out, None) == -1
+    assert L.rfdetr_b200_wait(None) == -1
+    assert L.rfdetr_b200_forward_rgb(None, buf, 1, 2, 2, out, out, None) == -1
+    assert L.rfdetr_b200_enqueue_device(None, buf, 1, 2, 2) == -1
+    assert L.rfdetr_b200_sync(None) == -1
+
+
 def test_init_errors_without_touching_the_gpu(tmp_path):
     L = lib.lib()
     st = C.c_int(0)
