@@ -28,6 +28,9 @@
 
 namespace rfb {
 
+// Scratch for the split-K partial sums of LayerNorm GEMMs with few row blocks.
+constexpr size_t kSplitWsBytes = (size_t)8 << 20;
+
 namespace {
 
 uint16_t f2h_bits(float f) {
@@ -412,6 +415,9 @@ rfdetr_status Engine::alloc_activations(int B) {
         {(void**)&taps_, Mp * L_ * D_ * 2},
         {(void**)&cat_, Mp * (2 + bnecks_.size()) * Cb_ * 2},
         {(void**)&tmp128_, Mp * Cb_ * 2},
+        // split-K LayerNorm GEMMs run only with at most 74 tiles, so their partial sums never exceed
+        // 148 splits x 128 rows x 64 columns of floats, whatever the batch
+        {(void**)&splitws_, kSplitWsBytes},
         {(void**)&p32a_, Mp * Dm_ * 4},
         {(void**)&proj32_, Mp * Dm_ * 4},
         {(void**)&mem16_, Mp * Dm_ * 2},
@@ -481,6 +487,7 @@ namespace {
 struct Launcher {
     cudaStream_t st;
     int* err;
+    float* splitws = nullptr;  // scratch for split-K LayerNorm GEMMs (kSplitWsBytes)
     int count = 0;
     bool ok = true;
     // optional per-launch events (profiling)
@@ -518,6 +525,7 @@ struct Launcher {
         a.resid = resid; a.ldr = ldr;
         a.out32 = out32; a.ld32 = ld32; a.out16 = out16; a.ld16 = ld16;
         a.err = err;
+        if (splitws) { a.split_ws = splitws; a.split_ws_bytes = kSplitWsBytes; }
         check(rfb::gemm(a, st), what);
     }
     // ConvX: 3x3 convolution (implicit GEMM over the channels-last map `src`,
@@ -532,6 +540,7 @@ struct Launcher {
         a.ln_g = ln->g; a.ln_b = ln->b; a.ln_eps = eps;
         a.out16 = out16; a.ld16 = ld16;
         a.err = err;
+        if (splitws) { a.split_ws = splitws; a.split_ws_bytes = kSplitWsBytes; }
         check(rfb::gemm(a, st), what);
     }
 };
@@ -594,6 +603,7 @@ rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int 
     if (B <= 0 || B > max_batch_) return RFDETR_ERR_INVALID_ARG;
     if (RFB_CUDA_FAIL(cudaSetDevice(device_))) return RFDETR_ERR_INFERENCE;
     Launcher L{stream_, d_err_};
+    L.splitws = splitws_;
     if (profiling_) {
         L.ev = &prof_ev_;
         L.names = &prof_names_;

@@ -171,6 +171,7 @@ private:
     __half* taps_ = nullptr;
     __half* cat_ = nullptr;
     __half* tmp128_ = nullptr;
+    float* splitws_ = nullptr;  // split-K partial sums of the LayerNorm GEMMs with few row blocks
     float* p32a_ = nullptr;
     float* proj32_ = nullptr;
     __half* mem16_ = nullptr;

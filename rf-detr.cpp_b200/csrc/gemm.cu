@@ -12,6 +12,7 @@
 // Every mbarrier wait is bounded; on timeout the CTA records an error word and
 // unwinds (no trap, no endless spin).
 #include "gemm.cuh"
+#include "kernels.cuh"
 #include "epilogue.cuh"
 #include "sm100.cuh"
 
@@ -144,7 +145,9 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 const int cimg = CONV ? mt / conv_tpi : 0;
                 const int cy0 = CONV ? (mt - cimg * conv_tpi) * p.conv_r : 0;
                 const int cch = CONV ? p.conv_c / BK : 1;  // 64-channel chunks per tap
-                for (int kb = 0; kb < num_kb; ++kb) {
+                const int kb0 = p.kb_per ? b * p.kb_per : 0;
+                const int kb1 = p.kb_per ? min(num_kb, kb0 + p.kb_per) : num_kb;
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait<CTA2>(&empty[stage], phase ^ 1, cta_abort, p.err)) goto done;
                     if constexpr (CTA2) {
                         if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);  // both halves
@@ -189,7 +192,9 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                 if (!mbar_wait<CTA2>(&tempty[acc], acc_phase ^ 1, cta_abort, p.err)) goto done;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                const int kb0 = p.kb_per ? (tile / tiles_per_batch) * p.kb_per : 0;
+                const int kb1 = p.kb_per ? min(num_kb, kb0 + p.kb_per) : num_kb;
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait<CTA2>(&full[stage], phase, cta_abort, p.err)) goto done;
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
@@ -200,8 +205,9 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         for (int sp = 0; sp < C::NSPLIT; ++sp) {
                             const uint64_t ad = sw128_kmajor_desc(a0 + kk * 32);
                             const uint64_t bd = sw128_kmajor_desc(b0 + sp * C::HSLAB * 128 + kk * 32);
-                            if constexpr (CTA2) umma_f16_pair(d_tmem + sp * C::SLAB, ad, bd, IDESC, (kb | kk) != 0);
-                            else umma_f16(d_tmem + sp * C::SLAB, ad, bd, IDESC, (kb | kk) != 0);
+                            const uint32_t accum = (kb > kb0 || kk > 0) ? 1u : 0u;
+                            if constexpr (CTA2) umma_f16_pair(d_tmem + sp * C::SLAB, ad, bd, IDESC, accum);
+                            else umma_f16(d_tmem + sp * C::SLAB, ad, bd, IDESC, accum);
                         }
                     }
                     if constexpr (CTA2) {
@@ -712,7 +718,9 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     const long long b_rows = (long long)a.b_batch_rows * (a.batches - 1) + a.N;
     if constexpr (CONV) {
         a.conv_r = BM / a.conv_w;
-        if (a.batches != 1 || a.conv_r < 1 || a.K != 9 * a.conv_c || a.M % (a.conv_h * a.conv_w)) return cudaErrorInvalidValue;
+        // batches > 1 only as split-K partial sums of one convolution (kb_per > 0)
+        if ((a.batches != 1 && !a.kb_per) || a.conv_r < 1 || a.K != 9 * a.conv_c || a.M % (a.conv_h * a.conv_w))
+            return cudaErrorInvalidValue;
         if (!make_conv_map(&ta, a.conv_src, a.conv_c, a.conv_w, a.conv_h, a.M / (a.conv_h * a.conv_w), a.conv_lds,
                            a.conv_r))
             return cudaErrorInvalidValue;
@@ -776,6 +784,22 @@ bool use_pair(const GemmArgs& a, int bn) {
     return bn == 384 && tiles >= (long long)g_num_sms;
 }
 
+// RFDETR_GEMM_SPLITK=0 keeps the full-row LayerNorm tiles for few row blocks.
+bool splitk_enabled() {
+    const char* env = std::getenv("RFDETR_GEMM_SPLITK");
+    return !(env && env[0] == '0');
+}
+
+// What the split-K LayerNorm row kernel handles: rows of 128 / 256 / 384, no activation or SiLU,
+// 16-byte aligned f32 rows and 8-byte aligned f16 rows.
+bool splitk_ln_supported(const GemmArgs& a) {
+    auto al = [](const void* q, uintptr_t m) { return !((uintptr_t)q & m); };
+    return (a.N == 128 || a.N == 256 || a.N == 384) && (a.act == ACT_NONE || a.act == ACT_SILU) &&
+           al(a.split_ws, 15) && al(a.bias, 15) && al(a.colscale, 15) && al(a.ln_g, 15) && al(a.ln_b, 15) &&
+           (!a.resid || (al(a.resid, 15) && a.ldr % 4 == 0)) && (!a.out32 || (al(a.out32, 15) && a.ld32 % 4 == 0)) &&
+           (!a.out16 || (al(a.out16, 7) && a.ld16 % 4 == 0));
+}
+
 // Residual GEMMs of N = 384 and long K (the MLP's second linear) as one
 // 384-wide tile per row block; RFDETR_GEMM_BN384=0 falls back to two 192-wide tiles.
 bool wide_resid() {
@@ -825,6 +849,32 @@ cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
         if (a.epi != EPI_LN || (a.N != 128 && a.N != 256) || !a.ln_g || !a.ln_b || a.conv_c % BK || a.conv_w < 1 ||
             a.conv_w > BM || a.conv_h < 1 || (a.act != ACT_NONE && a.act != ACT_SILU))
             return cudaErrorInvalidValue;
+        if (a.split_ws && a.batches == 1 && splitk_enabled() && splitk_ln_supported(a)) {
+            // few row-tiles (small batches): split-K f32 partial sums + in-order LayerNorm rows, as below
+            const int num_kb = (a.K + BK - 1) / BK;
+            const int conv_r = BM / a.conv_w;
+            const long long tiles = (long long)((a.conv_h + conv_r - 1) / conv_r) * (a.M / (a.conv_h * a.conv_w));
+            if (tiles * 2 <= g_num_sms && num_kb >= 2) {
+                int ks = (int)(g_num_sms / tiles);
+                ks = ks < num_kb ? ks : num_kb;
+                const int kbp = (num_kb + ks - 1) / ks;
+                ks = (num_kb + kbp - 1) / kbp;
+                if (ks >= 2 && (size_t)ks * a.M * a.N * sizeof(float) <= a.split_ws_bytes) {
+                    GemmArgs s = a;
+                    s.epi = EPI_F32; s.act = ACT_NONE;
+                    s.bias = nullptr; s.ln_g = nullptr; s.ln_b = nullptr;
+                    s.out32 = a.split_ws; s.ld32 = a.N; s.out16 = nullptr; s.ld16 = 0;
+                    s.batches = ks; s.a_batch_rows = 0; s.b_batch_rows = 0;
+                    s.out_batch_stride = (long long)a.M * a.N;
+                    s.kb_per = kbp;
+                    const cudaError_t e = a.N == 256 ? launch<256, EPI_F32, ACT_NONE, true>(s, stream)
+                                                     : launch<128, EPI_F32, ACT_NONE, true>(s, stream);
+                    if (e != cudaSuccess) return e;
+                    return splitk_layernorm(a.split_ws, ks, (long long)a.M * a.N, a.M, a.N, a.bias, nullptr, nullptr,
+                                            0, a.ln_g, a.ln_b, a.ln_eps, a.act, 0, nullptr, 0, a.out16, a.ld16, stream);
+                }
+            }
+        }
         if (a.act == ACT_SILU)
             return a.N == 256 ? launch<256, EPI_LN, ACT_SILU, true>(a, stream) : launch<128, EPI_LN, ACT_SILU, true>(a, stream);
         return a.N == 256 ? launch<256, EPI_LN, ACT_NONE, true>(a, stream) : launch<128, EPI_LN, ACT_NONE, true>(a, stream);
@@ -845,6 +895,39 @@ cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
         bn = 128;
     } else {
         bn = 64;
+    }
+    if (a.epi == EPI_LN && a.split_ws && a.batches == 1 && splitk_enabled()) {
+        // Few row blocks (small batches): a full-row LayerNorm tile per row block would leave most
+        // SMs idle, so the K range is split: f32 partial sums per split into the scratch, then
+        // one row kernel adds them in split order and applies bias, scale, residual, LayerNorm and
+        // the activation (deterministic: the order of the additions is fixed).
+        const int num_kb = (a.K + BK - 1) / BK;
+        const long long m_tiles = (a.M + BM - 1) / BM;
+        int sbn = a.N % 256 == 0 ? 256 : (a.N % 192 == 0 ? 192 : (a.N > 64 ? 128 : 64));
+        for (const int w : {128, 64})
+            if (m_tiles * ((a.N + sbn - 1) / sbn) < g_num_sms && w < sbn) sbn = w;
+        const long long tiles = m_tiles * ((a.N + sbn - 1) / sbn);
+        if (tiles * 2 <= g_num_sms && num_kb >= 2 && splitk_ln_supported(a)) {
+            int ks = (int)(g_num_sms / tiles);
+            ks = ks < num_kb ? ks : num_kb;
+            const int kbp = (num_kb + ks - 1) / ks;
+            ks = (num_kb + kbp - 1) / kbp;  // no empty split
+            if (ks >= 2 && (size_t)ks * a.M * a.N * sizeof(float) <= a.split_ws_bytes) {
+                GemmArgs s = a;
+                s.epi = EPI_F32; s.act = ACT_NONE;
+                s.bias = nullptr; s.colscale = nullptr; s.resid = nullptr;
+                s.ln_g = nullptr; s.ln_b = nullptr; s.ln_pre32 = 0;
+                s.out32 = a.split_ws; s.ld32 = a.N; s.out16 = nullptr; s.ld16 = 0;
+                s.batches = ks; s.a_batch_rows = 0; s.b_batch_rows = 0;
+                s.out_batch_stride = (long long)a.M * a.N;
+                s.kb_per = kbp;
+                const cudaError_t e = dispatch_bn<EPI_F32, ACT_NONE>(s, sbn, stream);
+                if (e != cudaSuccess) return e;
+                return splitk_layernorm(a.split_ws, ks, (long long)a.M * a.N, a.M, a.N, a.bias, a.colscale, a.resid,
+                                        a.ldr, a.ln_g, a.ln_b, a.ln_eps, a.act, a.ln_pre32, a.out32, a.ld32, a.out16,
+                                        a.ld16, stream);
+            }
+        }
     }
     if (a.epi != EPI_LN) {
         // few row blocks (small batches): narrower tiles until the grid covers every SM, so a

@@ -34,6 +34,13 @@ struct GemmArgs {
     int batches = 1;
     int a_batch_rows = 0, b_batch_rows = 0;
     long long out_batch_stride = 0;  // elements
+    // kb_per > 0 (split-K): batch b covers k-blocks [b*kb_per, (b+1)*kb_per) of the same A and B rows
+    // (a_batch_rows = b_batch_rows = 0) and writes its partial sums to its own output slice
+    int kb_per = 0;
+    // EPI_LN with few row blocks: scratch for split-K partial sums (f32); when given and large enough
+    // the GEMM runs as split-K f32 partials plus an in-order reduction that applies the epilogue
+    float* split_ws = nullptr;
+    size_t split_ws_bytes = 0;
     // epilogue
     int epi = EPI_F16;
     int act = ACT_NONE;

@@ -773,6 +773,102 @@ cudaError_t write_cls_rows(float* x, const float* clsrow, int B, int NW, int T, 
     return cudaGetLastError();
 }
 
+// Split-K epilogue (see splitk_layernorm): warp per row, grid-strided, lane owns columns
+// 4 * (lane + 32 i) .. + 3.
+template <int NV>
+__global__ void __launch_bounds__(256) k_splitk_ln(const float* __restrict__ part, int S, long long sstride, int rows,
+                                                  const float* __restrict__ bias, const float* __restrict__ colscale,
+                                                  const float* resid, int ldr, const float* __restrict__ g,
+                                                  const float* __restrict__ bb, float eps, int silu, int pre32,
+                                                  float* out32, int ld32, __half* __restrict__ out16, int ld16) {
+    constexpr int D = 128 * NV;
+    const int lane = threadIdx.x & 31;
+    const int stride = gridDim.x * (blockDim.x >> 5);
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += stride) {
+        float4 v[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) v[i] = reinterpret_cast<const float4*>(part + (size_t)row * D)[lane + 32 * i];
+        for (int sp = 1; sp < S; ++sp) {
+            const float4* q = reinterpret_cast<const float4*>(part + sp * sstride + (size_t)row * D);
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const float4 u = q[lane + 32 * i];
+                v[i].x += u.x; v[i].y += u.y; v[i].z += u.z; v[i].w += u.w;
+            }
+        }
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c0 = 4 * (lane + 32 * i);
+            if (bias) {
+                const float4 u = *reinterpret_cast<const float4*>(bias + c0);
+                v[i].x += u.x; v[i].y += u.y; v[i].z += u.z; v[i].w += u.w;
+            }
+            if (colscale) {
+                const float4 u = *reinterpret_cast<const float4*>(colscale + c0);
+                v[i].x *= u.x; v[i].y *= u.y; v[i].z *= u.z; v[i].w *= u.w;
+            }
+            if (resid) {
+                const float4 u = *reinterpret_cast<const float4*>(resid + (size_t)row * ldr + c0);
+                v[i].x += u.x; v[i].y += u.y; v[i].z += u.z; v[i].w += u.w;
+            }
+            s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        }
+        const float mean = warp_sum(s) / (float)D;
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const float a = v[i].x - mean, b2 = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+            q += (a * a + b2 * b2) + (c * c + d * d);
+        }
+        const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)D + eps);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c0 = 4 * (lane + 32 * i);
+            const float4 gg = *reinterpret_cast<const float4*>(g + c0);
+            const float4 be = *reinterpret_cast<const float4*>(bb + c0);
+            float4 y;
+            y.x = (v[i].x - mean) * rstd * gg.x + be.x;
+            y.y = (v[i].y - mean) * rstd * gg.y + be.y;
+            y.z = (v[i].z - mean) * rstd * gg.z + be.z;
+            y.w = (v[i].w - mean) * rstd * gg.w + be.w;
+            if (silu) {
+                y.x = __fdividef(y.x, 1.0f + __expf(-y.x));
+                y.y = __fdividef(y.y, 1.0f + __expf(-y.y));
+                y.z = __fdividef(y.z, 1.0f + __expf(-y.z));
+                y.w = __fdividef(y.w, 1.0f + __expf(-y.w));
+            }
+            if (out32) *reinterpret_cast<float4*>(out32 + (size_t)row * ld32 + c0) = pre32 ? v[i] : y;
+            if (out16) {
+                __half2 h0 = __floats2half2_rn(y.x, y.y), h1 = __floats2half2_rn(y.z, y.w);
+                *reinterpret_cast<uint2*>(out16 + (size_t)row * ld16 + c0) =
+                    make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+            }
+        }
+    }
+}
+
+cudaError_t splitk_layernorm(const float* part, int S, long long sstride, int rows, int D, const float* bias,
+                             const float* colscale, const float* resid, int ldr, const float* g, const float* b,
+                             float eps, int act, int pre32, float* out32, int ld32, __half* out16, int ld16,
+                             cudaStream_t st) {
+    if (S < 1 || rows <= 0 || (act != 0 && act != 3) || !g || !b) return cudaErrorInvalidValue;
+    const unsigned blocks = cdiv(rows, 8) < 148u * 6u ? cdiv(rows, 8) : 148u * 6u;
+    const int silu = act == 3;
+    if (D == 384)
+        k_splitk_ln<3><<<blocks, 256, 0, st>>>(part, S, sstride, rows, bias, colscale, resid, ldr, g, b, eps, silu,
+                                               pre32, out32, ld32, out16, ld16);
+    else if (D == 256)
+        k_splitk_ln<2><<<blocks, 256, 0, st>>>(part, S, sstride, rows, bias, colscale, resid, ldr, g, b, eps, silu,
+                                               pre32, out32, ld32, out16, ld16);
+    else if (D == 128)
+        k_splitk_ln<1><<<blocks, 256, 0, st>>>(part, S, sstride, rows, bias, colscale, resid, ldr, g, b, eps, silu,
+                                               pre32, out32, ld32, out16, ld16);
+    else
+        return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
 cudaError_t layernorm(const float* x, int rows, int D, const float* g, const float* b, float eps, float* y32,
                       __half* y16, cudaStream_t st) {
     if (D > 512) return cudaErrorInvalidValue;

@@ -38,6 +38,14 @@ cudaError_t write_cls_rows(float* x, const float* clsrow, int B, int NW, int T, 
 
 // LN(x) * g + b over rows of D (f32 in); writes y32 and/or y16 (either may
 // be null; y32 may alias x).
+// Split-K epilogue of a LayerNorm GEMM: x = sum over s < S of part[s] (in order) + bias, times
+// colscale, plus resid; y = act(LayerNorm(x) * g + b); out32 = pre32 ? x : y, out16 = y.  Rows of
+// D = 128 / 256 / 384 (act: ACT_NONE or ACT_SILU).  out32 may alias resid.
+cudaError_t splitk_layernorm(const float* part, int S, long long sstride, int rows, int D, const float* bias,
+                             const float* colscale, const float* resid, int ldr, const float* g, const float* b,
+                             float eps, int act, int pre32, float* out32, int ld32, __half* out16, int ld16,
+                             cudaStream_t st);
+
 cudaError_t layernorm(const float* x, int rows, int D, const float* g, const float* b, float eps, float* y32,
                       __half* y16, cudaStream_t st);
 
