@@ -270,7 +270,9 @@ def main():
     # ---- end to end through the C API (pinned host buffers) -------------
     # rfdetr_b200_submit_rgb: every step uploads its images from host memory and
     # downloads its logits and boxes into host memory; the upload of step i+1
-    # overlaps the forward of step i (two alternating host output buffers)
+    # overlaps the forward of step i.  The outputs are not read here, so two
+    # alternating host buffers suffice (a caller reading them gives each
+    # submission of a group its own buffers and reads after rfdetr_b200_wait).
     h_imgs = torch.empty((B, S, S, 3), dtype=torch.uint8, pin_memory=True)
     h_imgs.numpy()[:] = imgs
     h_np = h_imgs.numpy()
