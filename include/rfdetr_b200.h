@@ -57,6 +57,14 @@ rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8_t* rgb, in
  * of any of them. */
 rfdetr_status rfdetr_b200_wait(rfdetr_context* ctx);
 
+/* Waits only for the oldest rfdetr_b200_submit_rgb not yet waited for: when it
+ * returns RFDETR_OK, that submission's outputs are in host memory and its
+ * input and output buffers may be reused, while later submissions keep
+ * running (a streaming loop: submit batch i+1, wait_oldest, read batch i).
+ * Returns RFDETR_OK at once when nothing is outstanding.  Device errors are
+ * reported by rfdetr_b200_wait. */
+rfdetr_status rfdetr_b200_wait_oldest(rfdetr_context* ctx);
+
 /* Same, from already-preprocessed planar input [batch][3][S][S] (S = image
  * size), i.e. exactly the `input` argument of rfdetr_model_forward. */
 rfdetr_status rfdetr_b200_forward_planar(rfdetr_context* ctx, const float* planar, int batch,

@@ -16,6 +16,7 @@
 #include "select.cuh"
 
 #include <algorithm>
+#include <deque>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -55,6 +56,9 @@ struct rfdetr_context {
     cudaEvent_t slot_ready[2] = {nullptr, nullptr};
     cudaEvent_t slot_free[2] = {nullptr, nullptr};
     int next_slot = 0;
+    // one event per outstanding submission (after its output copies), oldest first; spare events
+    std::deque<cudaEvent_t> inflight;
+    std::vector<cudaEvent_t> spare_events;
 
     ~rfdetr_context() {
         if (h_in) cudaFreeHost(h_in);
@@ -65,6 +69,8 @@ struct rfdetr_context {
         if (engine) cudaSetDevice(engine->device());
         if (copy_stream) cudaStreamSynchronize(copy_stream);
         if (engine) cudaStreamSynchronize(engine->stream());
+        for (cudaEvent_t ev : inflight) cudaEventDestroy(ev);
+        for (cudaEvent_t ev : spare_events) cudaEventDestroy(ev);
         for (int k = 0; k < 2; ++k) {
             if (d_slot[k]) cudaFree(d_slot[k]);
             if (slot_ready[k]) cudaEventDestroy(slot_ready[k]);
@@ -431,11 +437,40 @@ extern "C" rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8
     s = e.enqueue(batch, ctx->d_slot[k], width, height);
     if (s != RFDETR_OK) return s;
     if (RFB_CUDA_FAIL(cudaEventRecord(ctx->slot_free[k], e.stream()))) return RFDETR_ERR_INFERENCE;
-    return enqueue_output_copies(ctx, batch, out_logits, out_boxes, out_masks);
+    s = enqueue_output_copies(ctx, batch, out_logits, out_boxes, out_masks);
+    if (s != RFDETR_OK) return s;
+    cudaEvent_t done = nullptr;
+    if (!ctx->spare_events.empty()) {
+        done = ctx->spare_events.back();
+        ctx->spare_events.pop_back();
+    } else if (RFB_CUDA_FAIL(cudaEventCreateWithFlags(&done, cudaEventDisableTiming))) {
+        return RFDETR_ERR_INFERENCE;
+    }
+    if (RFB_CUDA_FAIL(cudaEventRecord(done, e.stream()))) {
+        ctx->spare_events.push_back(done);
+        return RFDETR_ERR_INFERENCE;
+    }
+    ctx->inflight.push_back(done);
+    return RFDETR_OK;
+}
+
+extern "C" rfdetr_status rfdetr_b200_wait_oldest(rfdetr_context* ctx) {
+    if (!ctx || !ctx->engine) return RFDETR_ERR_INVALID_ARG;
+    if (ctx->inflight.empty()) return RFDETR_OK;
+    if (RFB_CUDA_FAIL(cudaSetDevice(ctx->engine->device()))) return RFDETR_ERR_INFERENCE;
+    cudaEvent_t ev = ctx->inflight.front();
+    ctx->inflight.pop_front();
+    const bool ok = !RFB_CUDA_FAIL(cudaEventSynchronize(ev));
+    ctx->spare_events.push_back(ev);
+    return ok ? RFDETR_OK : RFDETR_ERR_INFERENCE;
 }
 
 extern "C" rfdetr_status rfdetr_b200_wait(rfdetr_context* ctx) {
     if (!ctx || !ctx->engine) return RFDETR_ERR_INVALID_ARG;
+    while (!ctx->inflight.empty()) {  // finished by the synchronizations below
+        ctx->spare_events.push_back(ctx->inflight.front());
+        ctx->inflight.pop_front();
+    }
     if (ctx->copy_stream) {
         if (RFB_CUDA_FAIL(cudaSetDevice(ctx->engine->device())) ||
             RFB_CUDA_FAIL(cudaStreamSynchronize(ctx->copy_stream)))

@@ -103,6 +103,7 @@ SIGNATURES = {
     "rfdetr_b200_submit_rgb": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                          C.c_void_p, C.c_void_p]),
     "rfdetr_b200_wait": (C.c_int, [C.c_void_p]),
+    "rfdetr_b200_wait_oldest": (C.c_int, [C.c_void_p]),
     "rfdetr_b200_device_outputs": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                              C.POINTER(C.c_void_p)]),
     "rfdetr_b200_detect_batch": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.c_size_t, C.POINTER(DetectParams),
@@ -238,6 +239,9 @@ class Engine:
 
     def wait(self):
         check(lib().rfdetr_b200_wait(self._ctx), "wait")
+
+    def wait_oldest(self):
+        check(lib().rfdetr_b200_wait_oldest(self._ctx), "wait_oldest")
 
     def trace(self, name: str, batch: int, size_hint: int = 1 << 26) -> np.ndarray:
         out = np.zeros(size_hint, np.float32)

@@ -198,6 +198,7 @@ def test_b200_entry_points_reject_null_handles():
     out = (C.c_float * 4)()
     assert L.rfdetr_b200_submit_rgb(None, buf, 1, 2, 2, out, out, None) == -1
     assert L.rfdetr_b200_wait(None) == -1
+    assert L.rfdetr_b200_wait_oldest(None) == -1
     assert L.rfdetr_b200_forward_rgb(None, buf, 1, 2, 2, out, out, None) == -1
     assert L.rfdetr_b200_enqueue_device(None, buf, 1, 2, 2) == -1
     assert L.rfdetr_b200_sync(None) == -1

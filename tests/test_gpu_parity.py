@@ -206,6 +206,31 @@ def test_pipelined_submissions_match_forward_rgb(make_model):
     eng.close()
 
 
+def test_streaming_submissions_wait_oldest(make_model):
+    """A streaming loop with rfdetr_b200_wait_oldest: submit batch i+1, wait for the oldest, read
+    batch i while i+1 runs; every batch equals the synchronous rfdetr_b200_forward_rgb."""
+    import torch
+    from rfdetr_b200 import lib
+
+    path = make_model("tiny", "f16", 0)
+    S = 128
+    eng = lib.Engine(path, max_batch=2)
+    batches = [_images(S, 2, 51 + i) for i in range(4)]
+    want = [eng.forward_rgb(x)[:2] for x in batches]
+    pinned = [torch.from_numpy(x).pin_memory() for x in batches]
+    outs = [(torch.empty((2, eng.nq, eng.nc), dtype=torch.float32).pin_memory(),
+             torch.empty((2, eng.nq, 4), dtype=torch.float32).pin_memory()) for _ in batches]
+    eng.submit_rgb(pinned[0].numpy(), outs[0][0].numpy(), outs[0][1].numpy())
+    for i in range(len(batches)):
+        if i + 1 < len(batches):
+            eng.submit_rgb(pinned[i + 1].numpy(), outs[i + 1][0].numpy(), outs[i + 1][1].numpy())
+        eng.wait_oldest()  # batch i is complete
+        assert np.array_equal(outs[i][0].numpy(), want[i][0]) and np.array_equal(outs[i][1].numpy(), want[i][1])
+    eng.wait_oldest()  # nothing outstanding: returns at once
+    eng.wait()
+    eng.close()
+
+
 # Every configuration the benchmark description names, at its real model size
 # (batch 2: the oracle checks both images; the full batches run through the
 # same kernels, only more rows).
