@@ -93,7 +93,8 @@ typedef struct rfdetr_b200_det {
 
 /* Batched rfdetr_detect: n images (any sizes) -> per-image detection arrays.
  * out_dets[i] / out_counts[i] follow rfdetr_detect's ownership rules
- * (free each with rfdetr_detections_free). */
+ * (free each with rfdetr_detections_free).  On an error every out_dets[i] is
+ * NULL and every out_counts[i] 0: nothing is left to free. */
 rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfdetr_image* const* imgs, size_t n,
                                        const rfdetr_detect_params* params, rfdetr_detection** out_dets,
                                        size_t* out_counts);
@@ -180,6 +181,13 @@ int rfdetr_b200_op_quantize(int type, const float* d_src, long long n, void* d_o
 int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes, int batch, int nq, int nc, float threshold,
                           int top_k, const uint32_t* d_class_filter, int filter_len, int img_w, int img_h,
                           rfdetr_b200_det* d_out, int* d_counts, void* stream);
+
+/* Two-stage query selection (src/rfdetr_model.cpp:39-62, top_k_by_max_class):
+ * for each image b, the k of its n tokens with the largest maximum class logit
+ * (d_cls f32 [batch][n][nc]), in descending order of that maximum (ties: lower
+ * token first; the reference's partial_sort leaves tie order unspecified) ->
+ * d_idx int32 [batch][k].  1 <= n <= 4096, 0 <= k <= n.  Device pointers. */
+int rfdetr_b200_op_topk(const float* d_cls, int batch, int n, int nc, int k, int32_t* d_idx, void* stream);
 
 /* 32-bit words of one bit-packed img_w x img_h mask (rows padded to 32 pixels). */
 size_t rfdetr_b200_mask_bits_words(int img_w, int img_h);

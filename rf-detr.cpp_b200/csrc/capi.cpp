@@ -208,6 +208,22 @@ rfdetr_status forward_rgb_impl(rfdetr_context* ctx, const uint8_t* h_rgb, int ba
     return e.finish();
 }
 
+// Release the detection arrays of out_dets[0..n) and clear them (error paths:
+// a failed call hands back no arrays).
+void release_results(rfdetr_detection** out_dets, size_t* out_counts, size_t n) {
+    for (size_t i = 0; i < n; ++i) {
+        rfdetr_detections_free(out_dets[i], out_counts[i]);
+        out_dets[i] = nullptr;
+        out_counts[i] = 0;
+    }
+}
+
+// An image whose pixel buffer holds exactly width x height RGB triples.
+bool image_ok(const rfdetr_image* img) {
+    return img && img->width > 0 && img->height > 0 &&
+           img->rgb.size() == (size_t)img->width * (size_t)img->height * 3;
+}
+
 void attach_names(const rfdetr_context* ctx, rfdetr_detection* d, size_t n) {
     const auto& names = ctx->model->cfg.class_names;
     for (size_t i = 0; i < n; ++i)
@@ -303,7 +319,10 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
         out_counts[b] = 0;
         if (n <= 0) continue;
         auto* d = static_cast<rfdetr_detection*>(std::calloc((size_t)n, sizeof(rfdetr_detection)));
-        if (!d) return RFDETR_ERR_OUT_OF_MEMORY;
+        if (!d) {
+            release_results(out_dets, out_counts, (size_t)b);
+            return RFDETR_ERR_OUT_OF_MEMORY;
+        }
         for (int i = 0; i < n; ++i) {
             const rfdetr_b200_det& r = ctx->h_dets[(size_t)b * nq + i];
             d[i].class_id = (uint32_t)r.class_id;
@@ -366,7 +385,7 @@ extern "C" rfdetr_status rfdetr_detect(rfdetr_context* ctx, const rfdetr_image* 
     if (out_detections) *out_detections = nullptr;
     if (out_n) *out_n = 0;
     if (!ctx || !img || !params || !out_detections || !out_n) return RFDETR_ERR_INVALID_ARG;
-    if (!ctx->engine || img->width <= 0 || img->height <= 0 || img->rgb.empty()) return RFDETR_ERR_INVALID_ARG;
+    if (!ctx->engine || !image_ok(img)) return RFDETR_ERR_INVALID_ARG;
     const size_t bytes = img->rgb.size();
     if (!ctx->stage_in(bytes)) return RFDETR_ERR_OUT_OF_MEMORY;
     std::memcpy(ctx->h_in, img->rgb.data(), bytes);
@@ -524,22 +543,30 @@ extern "C" rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfd
     if (!ctx || !ctx->engine || !imgs || !params || !out_dets || !out_counts) return RFDETR_ERR_INVALID_ARG;
     for (size_t i = 0; i < n; ++i) { out_dets[i] = nullptr; out_counts[i] = 0; }
     if (n == 0) return RFDETR_OK;
+    for (size_t i = 0; i < n; ++i)
+        if (!image_ok(imgs[i])) return RFDETR_ERR_INVALID_ARG;
     // Same-sized runs go through one batched forward; the preprocess kernel
-    // resizes each run to the model resolution on the GPU.
+    // resizes each run to the model resolution on the GPU.  A failure releases
+    // the arrays of the runs before it.
     size_t i = 0;
     while (i < n) {
-        if (!imgs[i] || imgs[i]->rgb.empty()) return RFDETR_ERR_INVALID_ARG;
         const int w = imgs[i]->width, h = imgs[i]->height;
         size_t j = i + 1;
-        while (j < n && imgs[j] && imgs[j]->width == w && imgs[j]->height == h) ++j;
+        while (j < n && imgs[j]->width == w && imgs[j]->height == h) ++j;
         const int batch = (int)(j - i);
         const size_t img_bytes = (size_t)w * h * 3;
-        if (!ctx->stage_in(img_bytes * batch)) return RFDETR_ERR_OUT_OF_MEMORY;
-        for (size_t k = i; k < j; ++k) std::memcpy(ctx->h_in + (k - i) * img_bytes, imgs[k]->rgb.data(), img_bytes);
-        rfdetr_status s = forward_rgb_impl(ctx, ctx->h_in, batch, w, h);
-        if (s != RFDETR_OK) return RFDETR_ERR_INFERENCE;
-        s = postprocess_device(ctx, batch, w, h, params, out_dets + i, out_counts + i);
-        if (s != RFDETR_OK) return s;
+        rfdetr_status s = RFDETR_OK;
+        if (!ctx->stage_in(img_bytes * batch)) {
+            s = RFDETR_ERR_OUT_OF_MEMORY;
+        } else {
+            for (size_t k = i; k < j; ++k) std::memcpy(ctx->h_in + (k - i) * img_bytes, imgs[k]->rgb.data(), img_bytes);
+            if (forward_rgb_impl(ctx, ctx->h_in, batch, w, h) != RFDETR_OK) s = RFDETR_ERR_INFERENCE;
+            else s = postprocess_device(ctx, batch, w, h, params, out_dets + i, out_counts + i);
+        }
+        if (s != RFDETR_OK) {
+            release_results(out_dets, out_counts, i);
+            return s;
+        }
         i = j;
     }
     return RFDETR_OK;

@@ -418,42 +418,34 @@ __global__ void __launch_bounds__(1024) k_topk(const float* __restrict__ cls, in
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     int P = 1;
     while (P < N) P <<= 1;
+    for (int t = N + threadIdx.x; t < P; t += blockDim.x) keys[t] = ~0ull;  // padding sorts last
     if (NC <= 96) {
-        // 8 tokens per warp at a time, every class load issued before the reductions: the
-        // row maxima are bound by load latency, not bandwidth
+        // 8 tokens per warp at a time: all 24 class loads of a round are issued before the first
+        // reduction consumes one (the row index is clamped instead of branched on, so no load
+        // waits behind another token's maximum); the row maxima are bound by load latency
         constexpr int U = 8;
-        for (int t0 = warp * U; t0 < P; t0 += nwarps * U) {
-            float m[U];
+        for (int t0 = warp * U; t0 < N; t0 += nwarps * U) {
+            float v[U][3];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int t = t0 + u;
-                m[u] = -INFINITY;
-                if (t < N) {
-                    const float* r = cls + ((size_t)b * N + t) * NC;
+                const float* r = cls + ((size_t)b * N + min(t0 + u, N - 1)) * NC;
 #pragma unroll
-                    for (int j = 0; j < 3; ++j)
-                        if (lane + 32 * j < NC) m[u] = fmaxf(m[u], r[lane + 32 * j]);
-                }
+                for (int j = 0; j < 3; ++j) v[u][j] = lane + 32 * j < NC ? __ldg(r + lane + 32 * j) : -INFINITY;
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int t = t0 + u;
-                const float mu = warp_max(m[u]);
-                if (lane == 0 && t < P)
-                    keys[t] = t < N ? ((unsigned long long)(~float_order(mu)) << 32) | (unsigned)t : ~0ull;
+                const float mu = warp_max(fmaxf(fmaxf(v[u][0], v[u][1]), v[u][2]));
+                if (lane == 0 && t < N) keys[t] = ((unsigned long long)(~float_order(mu)) << 32) | (unsigned)t;
             }
         }
     } else {
-        for (int t = warp; t < P; t += nwarps) {
-            unsigned long long key = ~0ull;
-            if (t < N) {
-                const float* r = cls + ((size_t)b * N + t) * NC;
-                float m = -INFINITY;
-                for (int c = lane; c < NC; c += 32) m = fmaxf(m, r[c]);
-                m = warp_max(m);
-                key = ((unsigned long long)(~float_order(m)) << 32) | (unsigned)t;
-            }
-            if (lane == 0) keys[t] = key;
+        for (int t = warp; t < N; t += nwarps) {
+            const float* r = cls + ((size_t)b * N + t) * NC;
+            float m = -INFINITY;
+            for (int c = lane; c < NC; c += 32) m = fmaxf(m, r[c]);
+            m = warp_max(m);
+            if (lane == 0) keys[t] = ((unsigned long long)(~float_order(m)) << 32) | (unsigned)t;
         }
     }
     __syncthreads();
@@ -923,7 +915,8 @@ cudaError_t two_stage_boxes(const float* delta, int B, int G, float* bbox, cudaS
 }
 
 cudaError_t topk_tokens(const float* cls, int B, int N, int NC, int K, int32_t* idx, cudaStream_t st) {
-    if (N > kTopkMax || K > N) return cudaErrorInvalidValue;
+    if (!cls || !idx || B < 0 || N <= 0 || N > kTopkMax || NC <= 0 || K < 0 || K > N) return cudaErrorInvalidValue;
+    if (B == 0 || K == 0) return cudaSuccess;
     k_topk<<<B, 1024, 0, st>>>(cls, N, NC, K, idx);
     return cudaGetLastError();
 }

@@ -57,6 +57,11 @@ extern "C" int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes
                                               static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int rfdetr_b200_op_topk(const float* d_cls, int batch, int n, int nc, int k, int32_t* d_idx,
+                                   void* stream) {
+    return (int)rfb::topk_tokens(d_cls, batch, n, nc, k, d_idx, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" size_t rfdetr_b200_mask_bits_words(int img_w, int img_h) {
     return (img_w > 0 && img_h > 0) ? rfb::mask_bits_words(img_w, img_h) : 0;
 }

@@ -125,6 +125,7 @@ SIGNATURES = {
                                            C.c_void_p]),
     "rfdetr_b200_quantize_gguf": (C.c_int, [C.c_char_p, C.c_char_p, C.c_int, C.c_int]),
     "rfdetr_b200_op_quantize": (C.c_int, [C.c_int, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
+    "rfdetr_b200_op_topk": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "rfdetr_b200_op_select": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
                                         C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "rfdetr_b200_mask_bits_words": (C.c_size_t, [C.c_int, C.c_int]),

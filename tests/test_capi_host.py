@@ -202,6 +202,9 @@ def test_b200_entry_points_reject_null_handles():
     assert L.rfdetr_b200_forward_rgb(None, buf, 1, 2, 2, out, out, None) == -1
     assert L.rfdetr_b200_enqueue_device(None, buf, 1, 2, 2) == -1
     assert L.rfdetr_b200_sync(None) == -1
+    # operator argument checks come before any launch: cudaErrorInvalidValue (1)
+    assert L.rfdetr_b200_op_topk(None, 1, 1600, 91, 300, None, None) == 1
+    assert L.rfdetr_b200_detect_batch(None, None, 0, None, None, None) == -1
 
 
 def test_init_errors_without_touching_the_gpu(tmp_path):

@@ -310,3 +310,25 @@ def test_conv3x3_layernorm(oc, act, B, H, W, Cin, lds):
     assert L.rfdetr_b200_op_conv3x3(_p(xw), lds, B, H, W, Cin, _p(wk), oc, _p(g), _p(b), 1e-6, act, _p(out32), oc,
                                     _p(out16), oc, _p(ws), ws_bytes - 1, _stream()) != 0
 
+
+
+@pytest.mark.parametrize("B,N,NC,K", [(1, 1600, 91, 300), (3, 1225, 91, 300), (2, 4096, 91, 300), (2, 1600, 120, 300),
+                                      (1, 50, 91, 50), (2, 20, 91, 7), (1, 1, 91, 1), (2, 700, 1, 300)])
+def test_topk_by_max_class(B, N, NC, K):
+    """Two-stage token selection (src/rfdetr_model.cpp:39-62) through rfdetr_b200_op_topk: the K
+    tokens of largest class maximum in descending order, ties to the lower token.  Logits are
+    multiples of 1/8 in a narrow range, so most maxima tie and the tie order is exercised; no
+    logit is zero, so signed zeros cannot tie."""
+    rng = np.random.default_rng(N + NC)
+    cls = ((rng.integers(-40, 40, (B, N, NC)) + 0.5) / 8).astype(np.float32)
+    m = cls.max(-1)
+    want = np.stack([np.lexsort((np.arange(N), -m[b]))[:K] for b in range(B)]).astype(np.int32)
+    d_cls = torch.from_numpy(cls).cuda()
+    d_idx = torch.full((B, K), -1, dtype=torch.int32, device="cuda:0")
+    L = _lib()
+    assert L.rfdetr_b200_op_topk(_p(d_cls), B, N, NC, K, _p(d_idx), _stream()) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(d_idx.cpu().numpy(), want)
+    # sizes the kernel does not take are rejected before any launch
+    assert L.rfdetr_b200_op_topk(_p(d_cls), B, 4097, NC, K, _p(d_idx), _stream()) != 0
+    assert L.rfdetr_b200_op_topk(_p(d_cls), B, N, NC, N + 1, _p(d_idx), _stream()) != 0

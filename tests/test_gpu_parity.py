@@ -365,6 +365,55 @@ def test_detect_api_matches_oracle_selection(make_model):
         assert d[6] is not None
 
 
+def test_detect_batch_matches_per_run_forwards(make_model):
+    """rfdetr_b200_detect_batch over images of two sizes (a run of two, then one): each image's
+    records equal the oracle's selection from the forward of its run; an empty list returns OK,
+    and a missing image returns RFDETR_ERR_INVALID_ARG with every output cleared."""
+    import ctypes as C
+
+    import oracle as O
+    from rfdetr_b200 import lib
+
+    path = make_model("tiny", "f16", 0)
+    L = lib.lib()
+    eng = lib.Engine(path, max_batch=2)
+    rng = np.random.default_rng(17)
+    arrs = [rng.integers(0, 256, (200, 160, 3), dtype=np.uint8) for _ in range(2)]
+    arrs.append(rng.integers(0, 256, (96, 144, 3), dtype=np.uint8))
+    st = C.c_int(0)
+    imgs = [L.rfdetr_image_from_rgb_buffer(a.ctypes.data, a.shape[1], a.shape[0], C.byref(st)) for a in arrs]
+    assert all(imgs)
+    dp = lib.DetectParams(0.3, 10, None, 0)
+    dets = (C.POINTER(lib.Detection) * 3)()
+    counts = (C.c_size_t * 3)()
+    assert L.rfdetr_b200_detect_batch(eng.ctx, (C.c_void_p * 3)(*imgs), 3, C.byref(dp), dets, counts) == 0
+    got = [[(dets[b][i].class_id, dets[b][i].score, dets[b][i].x1, dets[b][i].y1, dets[b][i].x2, dets[b][i].y2)
+            for i in range(counts[b])] for b in range(3)]
+    for b in range(3):
+        L.rfdetr_detections_free(dets[b], counts[b])
+
+    lg2, bx2, _ = eng.forward_rgb(np.stack(arrs[:2]))
+    lg1, bx1, _ = eng.forward_rgb(arrs[2][None])
+    want = [O.select(lg2[0], bx2[0], 0.3, 10, 160, 200), O.select(lg2[1], bx2[1], 0.3, 10, 160, 200),
+            O.select(lg1[0], bx1[0], 0.3, 10, 144, 96)]
+    assert sum(len(g) for g in got) > 0
+    for g, (q, c, s, xy) in zip(got, want):
+        assert len(g) == len(q)
+        for d, ci, si, box in zip(g, c, s, xy):
+            assert d[0] == ci and abs(d[1] - si) < 1e-6
+            assert np.allclose(d[2:6], box, atol=1e-3)
+
+    assert L.rfdetr_b200_detect_batch(eng.ctx, (C.c_void_p * 1)(), 0, C.byref(dp), dets, counts) == 0
+    bad_dets = (C.POINTER(lib.Detection) * 2)()
+    bad_counts = (C.c_size_t * 2)(7, 7)
+    assert L.rfdetr_b200_detect_batch(eng.ctx, (C.c_void_p * 2)(imgs[0], None), 2, C.byref(dp), bad_dets,
+                                      bad_counts) == -1
+    assert not bad_dets[0] and not bad_dets[1] and list(bad_counts) == [0, 0]
+    for im in imgs:
+        L.rfdetr_image_free(im)
+    eng.close()
+
+
 def test_flat_capi_with_png_and_seg_masks(make_model, tmp_path):
     """LocalAI's flat API (rfdetr_capi_*) on a segmentation model: JSON
     envelope, accessors, two-call sizing, PNG masks at the image size, and
