@@ -411,19 +411,27 @@ __device__ __forceinline__ uint32_t float_order(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// One 1024-thread CTA per image.  Key of token t: (~order(max_c cls[t][c]) << 32) | t, so that
+// ascending keys are descending maxima with ties to the lower token, as the output wants.
+//  1. class maxima (the work is issue-bound on the CTA's one SM, so instructions are what count):
+//     a warp takes 8 tokens per round, issues its 24 class loads before any reduction, and
+//     reduces the 8 per-lane maxima with a transposed butterfly (9 shuffles for the 8 tokens);
+//  2. K < N: radix select of the K-th smallest key over 8-bit digits (the 4 score bytes, then
+//     the 2 low index bytes; N <= 4096 keeps index bits 16-31 zero) with warp-aggregated
+//     shared-memory histograms, and compaction of the K keys <= it to keys[0, K);
+//  3. bitonic sort of those K keys (padded to a power of two) instead of all N.
+// Keys are unique, so the result is the first K of the full (score desc, index asc) order.
 __global__ void __launch_bounds__(1024) k_topk(const float* __restrict__ cls, int N, int NC, int K,
                                                 int32_t* __restrict__ idx) {
     __shared__ unsigned long long keys[kTopkMax];
+    __shared__ unsigned hist[256];
+    __shared__ int s_digit, s_want, s_count;
     const int b = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    int P = 1;
-    while (P < N) P <<= 1;
-    for (int t = N + threadIdx.x; t < P; t += blockDim.x) keys[t] = ~0ull;  // padding sorts last
     if (NC <= 96) {
-        // 8 tokens per warp at a time: all 24 class loads of a round are issued before the first
-        // reduction consumes one (the row index is clamped instead of branched on, so no load
-        // waits behind another token's maximum); the row maxima are bound by load latency
         constexpr int U = 8;
+        const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+        const int mine = (h16 ? 4 : 0) + (h8 ? 2 : 0) + (h4 ? 1 : 0);  // token of this lane after the butterfly
         for (int t0 = warp * U; t0 < N; t0 += nwarps * U) {
             float v[U][3];
 #pragma unroll
@@ -432,12 +440,23 @@ __global__ void __launch_bounds__(1024) k_topk(const float* __restrict__ cls, in
 #pragma unroll
                 for (int j = 0; j < 3; ++j) v[u][j] = lane + 32 * j < NC ? __ldg(r + lane + 32 * j) : -INFINITY;
             }
+            float a[U];
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int t = t0 + u;
-                const float mu = warp_max(fmaxf(fmaxf(v[u][0], v[u][1]), v[u][2]));
-                if (lane == 0 && t < N) keys[t] = ((unsigned long long)(~float_order(mu)) << 32) | (unsigned)t;
-            }
+            for (int u = 0; u < U; ++u) a[u] = fmaxf(fmaxf(v[u][0], v[u][1]), v[u][2]);
+            // each exchange halves the tokens a lane holds: the lane keeps one half and receives
+            // its partner's values of that half
+            float a4[4], a2[2];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                a4[i] = fmaxf(h16 ? a[i + 4] : a[i], __shfl_xor_sync(0xffffffffu, h16 ? a[i] : a[i + 4], 16));
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+                a2[i] = fmaxf(h8 ? a4[i + 2] : a4[i], __shfl_xor_sync(0xffffffffu, h8 ? a4[i] : a4[i + 2], 8));
+            float m = fmaxf(h4 ? a2[1] : a2[0], __shfl_xor_sync(0xffffffffu, h4 ? a2[0] : a2[1], 4));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            const int t = t0 + mine;
+            if ((lane & 3) == 0 && t < N) keys[t] = ((unsigned long long)(~float_order(m)) << 32) | (unsigned)t;
         }
     } else {
         for (int t = warp; t < N; t += nwarps) {
@@ -448,6 +467,78 @@ __global__ void __launch_bounds__(1024) k_topk(const float* __restrict__ cls, in
             if (lane == 0) keys[t] = ((unsigned long long)(~float_order(m)) << 32) | (unsigned)t;
         }
     }
+    __syncthreads();
+    int P = 1;
+    if (K < N) {
+        const int jn = (N + blockDim.x - 1) / blockDim.x;  // keys per thread, <= 4
+        unsigned long long prefix = 0, mask = 0;
+        int want = K;  // rank of the wanted key among the keys that match prefix under mask
+#pragma unroll 1
+        for (int pass = 0; pass < 6; ++pass) {
+            const int sh = pass < 4 ? 56 - 8 * pass : 8 * (5 - pass);  // 56, 48, 40, 32, 8, 0
+            if (threadIdx.x < 256) hist[threadIdx.x] = 0;
+            __syncthreads();
+            for (int j = 0; j < jn; ++j) {
+                const int t = threadIdx.x + j * blockDim.x;
+                const unsigned long long key = t < N ? keys[t] : ~0ull;
+                const bool cand = t < N && (key & mask) == prefix;
+                const unsigned d = cand ? (unsigned)(key >> sh) & 255u : 256u;
+                const unsigned peers = __match_any_sync(0xffffffffu, d);
+                if (cand && lane == __ffs(peers) - 1) atomicAdd(&hist[d], (unsigned)__popc(peers));
+            }
+            __syncthreads();
+            if (warp == 0) {
+                unsigned c[8], sum = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    c[i] = hist[lane * 8 + i];
+                    sum += c[i];
+                }
+                unsigned incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += n;
+                }
+                const unsigned excl = incl - sum;
+                if (excl < (unsigned)want && (unsigned)want <= incl) {  // exactly one lane
+                    unsigned w = (unsigned)want - excl;
+                    int i = 0;
+                    for (; i < 7 && w > c[i]; ++i) w -= c[i];
+                    s_digit = lane * 8 + i;
+                    s_want = (int)w;
+                }
+            }
+            __syncthreads();
+            prefix |= (unsigned long long)s_digit << sh;
+            mask |= 255ull << sh;
+            want = s_want;
+        }
+        // prefix is now the K-th smallest key: keys <= prefix move to keys[0, K) (any order)
+        unsigned long long snap[kTopkMax / 1024];
+#pragma unroll
+        for (int j = 0; j < kTopkMax / 1024; ++j) {
+            const int t = threadIdx.x + j * blockDim.x;
+            snap[j] = j < jn && t < N ? keys[t] : ~0ull;
+        }
+        if (threadIdx.x == 0) s_count = 0;
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kTopkMax / 1024; ++j) {
+            if (j < jn) {
+                const bool sel = snap[j] <= prefix;
+                const unsigned bal = __ballot_sync(0xffffffffu, sel);
+                int base = 0;
+                if (lane == 0 && bal) base = atomicAdd(&s_count, __popc(bal));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (sel) keys[base + __popc(bal & ((1u << lane) - 1u))] = snap[j];
+            }
+        }
+        while (P < K) P <<= 1;
+    } else {
+        while (P < N) P <<= 1;
+    }
+    for (int t = min(K, N) + threadIdx.x; t < P; t += blockDim.x) keys[t] = ~0ull;  // padding sorts last
     __syncthreads();
     // bitonic sort ascending (smaller key = higher score, then lower index)
     if (P >= 64 && P <= 2 * (int)blockDim.x) {
