@@ -4,13 +4,16 @@
     python -m rfdetr_b200.kernels_bench attn --seq 1616 --groups 32 --heads 6 --hd 64
     python -m rfdetr_b200.kernels_bench deform --batch 32 --grid 40 --nq 300 --heads 16 --points 2
     python -m rfdetr_b200.kernels_bench mlp --m 51712 --n 384 --k 1536      (D = n, hidden F = k)
+    python -m rfdetr_b200.kernels_bench topk --batch 1 --grid 40 --nc 91 --nq 300
 
 Times `--iters` launches with CUDA events on the current stream (after
 `--warmup` launches) and prints one JSON line: ms per launch and achieved
 TFLOP/s (algorithmic FLOPs: 2*M*N*K for a GEMM, 4*L^2*hd per (group, head)
 for attention) or GB/s for the deformable sampling (algorithmic bytes: the
 value map read once, the offset/logit rows, the reference points and the f16
-output).  Used for ncu captures of one kernel in isolation.
+output) and the two-stage top-K (the grid x grid x nc f32 class logits of each
+image read once, the nq int32 indices written).  Used for ncu captures of one
+kernel in isolation.
 """
 import argparse
 import json
@@ -23,7 +26,7 @@ from . import lib
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "attn", "deform", "mlp"])
+    ap.add_argument("op", choices=["gemm", "attn", "deform", "mlp", "topk"])
     ap.add_argument("--m", type=int, default=51712)
     ap.add_argument("--n", type=int, default=1536)
     ap.add_argument("--k", type=int, default=384)
@@ -38,6 +41,7 @@ def main():
     ap.add_argument("--nq", type=int, default=300)
     ap.add_argument("--points", type=int, default=2)
     ap.add_argument("--dm", type=int, default=256)
+    ap.add_argument("--nc", type=int, default=91)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
@@ -89,6 +93,16 @@ def main():
             assert rc == 0, rc
         nbytes = value.numel() * 2 + so_aw.numel() * 4 + refp.numel() * 4 + out.numel() * 2
         name = f"deform batch={B} grid={G} nq={NQ} heads={H} points={P} dm={Dm}"
+    elif a.op == "topk":
+        B, N, NC, K = a.batch, a.grid * a.grid, a.nc, a.nq
+        cls = torch.randn(B, N, NC, device=dev, generator=g)
+        idx = torch.empty(B, K, dtype=torch.int32, device=dev)
+
+        def run():
+            rc = L.rfdetr_b200_op_topk(cls.data_ptr(), B, N, NC, K, idx.data_ptr(), st)
+            assert rc == 0, rc
+        nbytes = cls.numel() * 4 + idx.numel() * 4
+        name = f"topk batch={B} tokens={N} classes={NC} k={K}"
     else:
         D = a.heads * a.hd
         qkv = torch.randn(a.groups * a.seq, 3 * D, device=dev, generator=g).half()
@@ -111,7 +125,7 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.iters
-    if a.op == "deform":
+    if a.op in ("deform", "topk"):
         print(json.dumps({"op": name, "ms": round(ms, 5), "gbs": round(nbytes / ms / 1e6, 1),
                           "bytes": nbytes}))
     else:
