@@ -47,6 +47,8 @@ struct rfdetr_context {
     int* h_counts = nullptr;
     uint32_t* h_bits = nullptr;
     size_t h_dets_cap = 0, h_counts_cap = 0, h_bits_cap = 0;
+    int* h_err = nullptr;  // the forward's device error word, copied back with the detections
+    size_t h_err_cap = 0;
     // pipelined submissions (rfdetr_b200_submit_rgb): two device input slots
     // filled on a copy stream; the forward and the output copies run on the
     // engine stream behind slot_ready, and slot_free marks the slot's last reader
@@ -66,6 +68,7 @@ struct rfdetr_context {
         if (h_dets) cudaFreeHost(h_dets);
         if (h_counts) cudaFreeHost(h_counts);
         if (h_bits) cudaFreeHost(h_bits);
+        if (h_err) cudaFreeHost(h_err);
         if (engine) cudaSetDevice(engine->device());
         if (copy_stream) cudaStreamSynchronize(copy_stream);
         if (engine) cudaStreamSynchronize(engine->stream());
@@ -224,6 +227,30 @@ bool image_ok(const rfdetr_image* img) {
            img->rgb.size() == (size_t)img->width * (size_t)img->height * 3;
 }
 
+// Upload n images of img_bytes each to the engine's device input buffer, back to
+// back, through the pinned staging buffer in chunks: the host copy of a chunk
+// overlaps the DMA of the one before it.
+rfdetr_status upload_images(rfdetr_context* ctx, const rfdetr_image* const* imgs, size_t n, size_t img_bytes) {
+    rfb::Engine& e = *ctx->engine;
+    const size_t total = img_bytes * n;
+    if (RFB_CUDA_FAIL(cudaSetDevice(e.device()))) return RFDETR_ERR_INFERENCE;
+    if (!ctx->stage_in(total)) return RFDETR_ERR_OUT_OF_MEMORY;
+    const rfdetr_status s = e.reserve_rgb(total);
+    if (s != RFDETR_OK) return s;
+    constexpr size_t kChunk = 256u << 10;
+    for (size_t i = 0; i < n; ++i) {
+        const uint8_t* src = imgs[i]->rgb.data();
+        for (size_t off = 0; off < img_bytes; off += kChunk) {
+            const size_t len = std::min(kChunk, img_bytes - off), at = i * img_bytes + off;
+            std::memcpy(ctx->h_in + at, src + off, len);
+            if (RFB_CUDA_FAIL(cudaMemcpyAsync(e.d_rgb() + at, ctx->h_in + at, len, cudaMemcpyHostToDevice,
+                                              e.stream())))
+                return RFDETR_ERR_INFERENCE;
+        }
+    }
+    return RFDETR_OK;
+}
+
 void attach_names(const rfdetr_context* ctx, rfdetr_detection* d, size_t n) {
     const auto& names = ctx->model->cfg.class_names;
     for (size_t i = 0; i < n; ++i)
@@ -258,10 +285,13 @@ struct MaskExpand {
 };
 const MaskExpand g_mask_expand;
 
-// Post-process the last forward of `batch` images of w x h pixels on the
-// device (select.cu) and build the per-image rfdetr_detection arrays: only the
-// selected records and their bit masks cross PCIe; the 0/255 masks of the
-// reference API are expanded from the bits on the host.
+// Post-process the forward of `batch` images of w x h pixels queued last on
+// the engine stream, on the device (select.cu), and build the per-image
+// rfdetr_detection arrays: only the selected records and their bit masks cross
+// PCIe; the 0/255 masks of the reference API are expanded from the bits on the
+// host.  The forward's device error word comes back with the records, so the
+// forward and the selection share one synchronization; a nonzero word fails
+// the call before any array is built.
 rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, const rfdetr_detect_params* params,
                                  rfdetr_detection** out_dets, size_t* out_counts) {
     rfb::Engine& e = *ctx->engine;
@@ -278,9 +308,12 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
         (flen && !rfdetr_context::grow_dev(&ctx->d_filter, &ctx->filter_cap, flen)) ||
         (seg && !rfdetr_context::grow_dev(&ctx->d_bits, &ctx->bits_cap, (size_t)batch * max_dets * words)) ||
         !rfdetr_context::grow_host(&ctx->h_dets, &ctx->h_dets_cap, (size_t)batch * nq) ||
-        !rfdetr_context::grow_host(&ctx->h_counts, &ctx->h_counts_cap, (size_t)batch))
+        !rfdetr_context::grow_host(&ctx->h_counts, &ctx->h_counts_cap, (size_t)batch) ||
+        !rfdetr_context::grow_host(&ctx->h_err, &ctx->h_err_cap, 1))
         return RFDETR_ERR_OUT_OF_MEMORY;
     const cudaStream_t st = e.stream();
+    *ctx->h_err = 0;
+    if (e.enqueue_error_copy(ctx->h_err) != RFDETR_OK) return RFDETR_ERR_INFERENCE;
     if (flen && RFB_CUDA_FAIL(cudaMemcpyAsync(ctx->d_filter, params->class_filter, flen * 4, cudaMemcpyHostToDevice, st)))
         return RFDETR_ERR_INFERENCE;
     if (RFB_CUDA_FAIL(rfb::select_detections_device(e.logits(), e.boxes(), batch, nq, nc, params->threshold,
@@ -296,6 +329,7 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
                                       cudaMemcpyDeviceToHost, st)) ||
         RFB_CUDA_FAIL(cudaStreamSynchronize(st)))
         return RFDETR_ERR_INFERENCE;
+    if (e.device_error(*ctx->h_err) != RFDETR_OK) return RFDETR_ERR_INFERENCE;
     size_t kept = 0;
     for (int b = 0; b < batch; ++b) kept += (size_t)ctx->h_counts[b];
     if (seg && kept) {
@@ -386,17 +420,13 @@ extern "C" rfdetr_status rfdetr_detect(rfdetr_context* ctx, const rfdetr_image* 
     if (out_n) *out_n = 0;
     if (!ctx || !img || !params || !out_detections || !out_n) return RFDETR_ERR_INVALID_ARG;
     if (!ctx->engine || !image_ok(img)) return RFDETR_ERR_INVALID_ARG;
-    const size_t bytes = img->rgb.size();
-    if (!ctx->stage_in(bytes)) return RFDETR_ERR_OUT_OF_MEMORY;
-    std::memcpy(ctx->h_in, img->rgb.data(), bytes);
-    rfdetr_status s = forward_rgb_impl(ctx, ctx->h_in, 1, img->width, img->height);
+    rfb::Engine& e = *ctx->engine;
+    rfdetr_status s = e.reserve(1);
+    if (s == RFDETR_OK) s = upload_images(ctx, &img, 1, img->rgb.size());
+    if (s == RFDETR_OK) s = e.enqueue(1, e.d_rgb(), img->width, img->height);
+    if (s == RFDETR_OK) s = postprocess_device(ctx, 1, img->width, img->height, params, out_detections, out_n);
     if (s != RFDETR_OK) {
-        rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_detect: model forward failed");
-        return RFDETR_ERR_INFERENCE;
-    }
-    s = postprocess_device(ctx, 1, img->width, img->height, params, out_detections, out_n);
-    if (s != RFDETR_OK) {
-        rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_detect: post-processing failed");
+        rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_detect: inference failed");
         return s == RFDETR_ERR_OUT_OF_MEMORY ? s : RFDETR_ERR_INFERENCE;
     }
     return RFDETR_OK;
@@ -554,15 +584,12 @@ extern "C" rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfd
         size_t j = i + 1;
         while (j < n && imgs[j]->width == w && imgs[j]->height == h) ++j;
         const int batch = (int)(j - i);
-        const size_t img_bytes = (size_t)w * h * 3;
-        rfdetr_status s = RFDETR_OK;
-        if (!ctx->stage_in(img_bytes * batch)) {
-            s = RFDETR_ERR_OUT_OF_MEMORY;
-        } else {
-            for (size_t k = i; k < j; ++k) std::memcpy(ctx->h_in + (k - i) * img_bytes, imgs[k]->rgb.data(), img_bytes);
-            if (forward_rgb_impl(ctx, ctx->h_in, batch, w, h) != RFDETR_OK) s = RFDETR_ERR_INFERENCE;
-            else s = postprocess_device(ctx, batch, w, h, params, out_dets + i, out_counts + i);
-        }
+        rfb::Engine& e = *ctx->engine;
+        rfdetr_status s = e.reserve(batch);
+        if (s == RFDETR_OK) s = upload_images(ctx, imgs + i, (size_t)batch, (size_t)w * h * 3);
+        if (s == RFDETR_OK) s = e.enqueue(batch, e.d_rgb(), w, h);
+        if (s == RFDETR_OK) s = postprocess_device(ctx, batch, w, h, params, out_dets + i, out_counts + i);
+        if (s != RFDETR_OK && s != RFDETR_ERR_OUT_OF_MEMORY) s = RFDETR_ERR_INFERENCE;
         if (s != RFDETR_OK) {
             release_results(out_dets, out_counts, i);
             return s;

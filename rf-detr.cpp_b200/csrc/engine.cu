@@ -802,17 +802,25 @@ rfdetr_status Engine::finish() {
     if (RFB_CUDA_FAIL(cudaStreamSynchronize(stream_))) return RFDETR_ERR_INFERENCE;
     int err = 0;
     if (RFB_CUDA_FAIL(cudaMemcpy(&err, d_err_, sizeof(int), cudaMemcpyDeviceToHost))) return RFDETR_ERR_INFERENCE;
-    if (err) {
-        if ((err & 0xFF) == kErrWaitTimeout)
-            rfdetr_logf(RFDETR_LOG_ERROR,
-                        "forward: a kernel's bounded wait expired (mbarrier at shared offset 0x%x, cluster rank %d)",
-                        (unsigned)((err >> 8) & 0xFFFFF), (err >> 28) & 1);
-        else
-            rfdetr_logf(RFDETR_LOG_ERROR, "forward: device error word %d", err);
-        cudaMemset(d_err_, 0, sizeof(int));
-        return RFDETR_ERR_INFERENCE;
-    }
-    return RFDETR_OK;
+    return device_error(err);
+}
+
+rfdetr_status Engine::enqueue_error_copy(int* h_err) {
+    return RFB_CUDA_FAIL(cudaMemcpyAsync(h_err, d_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_))
+               ? RFDETR_ERR_INFERENCE
+               : RFDETR_OK;
+}
+
+rfdetr_status Engine::device_error(int err) {
+    if (!err) return RFDETR_OK;
+    if ((err & 0xFF) == kErrWaitTimeout)
+        rfdetr_logf(RFDETR_LOG_ERROR,
+                    "forward: a kernel's bounded wait expired (mbarrier at shared offset 0x%x, cluster rank %d)",
+                    (unsigned)((err >> 8) & 0xFFFFF), (err >> 28) & 1);
+    else
+        rfdetr_logf(RFDETR_LOG_ERROR, "forward: device error word %d", err);
+    cudaMemset(d_err_, 0, sizeof(int));
+    return RFDETR_ERR_INFERENCE;
 }
 
 long long Engine::trace(const std::string& name, int B, float* out, size_t cap) {

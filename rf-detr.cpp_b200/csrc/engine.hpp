@@ -60,6 +60,13 @@ public:
     rfdetr_status enqueue(int batch, const uint8_t* d_src_rgb, int src_w, int src_h);
     // Synchronize the stream and check the device error word.
     rfdetr_status finish();
+    // The same check in two halves, for callers that queue more work behind
+    // the forward before they synchronize: enqueue_error_copy() copies the
+    // device error word to `h_err` (pinned host memory) on the engine stream;
+    // after the synchronization, device_error(*h_err) logs and clears a
+    // nonzero word and reports it as RFDETR_ERR_INFERENCE.
+    rfdetr_status enqueue_error_copy(int* h_err);
+    rfdetr_status device_error(int err);
 
     // Outputs of the last forward (device pointers).
     const float* logits() const { return logits_; }   // [B*NQ][NC]
