@@ -45,8 +45,9 @@ rfdetr_status rfdetr_b200_forward_rgb(rfdetr_context* ctx, const uint8_t* rgb, i
 /* Pipelined form of rfdetr_b200_forward_rgb for a stream of batches: enqueues
  * the host-to-device copy of `rgb` (on a copy stream, into one of two device
  * input slots), the forward (behind that copy) and the device-to-host copies
- * of the outputs, and returns without waiting, so the upload of the next batch
- * overlaps the forward of this one.  `rgb` and the output buffers must stay
+ * of the outputs (from a device copy of them, on a third stream), and returns
+ * without waiting, so the upload of the next batch and the download of the
+ * previous one overlap the forward of this one.  `rgb` and the output buffers must stay
  * valid and untouched until rfdetr_b200_wait returns; page-locked host memory
  * is needed for the copies to overlap (pageable memory works, serialized).
  * Outputs as for rfdetr_b200_forward_rgb. */

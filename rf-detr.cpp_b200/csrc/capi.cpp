@@ -50,14 +50,22 @@ struct rfdetr_context {
     int* h_err = nullptr;  // the forward's device error word, copied back with the detections
     size_t h_err_cap = 0;
     // pipelined submissions (rfdetr_b200_submit_rgb): two device input slots
-    // filled on a copy stream; the forward and the output copies run on the
-    // engine stream behind slot_ready, and slot_free marks the slot's last reader
+    // filled on a copy stream; the forward runs on the engine stream behind
+    // slot_ready, and slot_free marks the slot's last reader
     cudaStream_t copy_stream = nullptr;
     uint8_t* d_slot[2] = {nullptr, nullptr};
     size_t slot_cap[2] = {0, 0};
     cudaEvent_t slot_ready[2] = {nullptr, nullptr};
     cudaEvent_t slot_free[2] = {nullptr, nullptr};
     int next_slot = 0;
+    // outputs of submission slot k: copied on the device into d_out[k] behind the
+    // forward (out_ready), then to the caller on d2h_stream (out_free), so the
+    // next forward does not wait for the PCIe transfer
+    cudaStream_t d2h_stream = nullptr;
+    uint8_t* d_out[2] = {nullptr, nullptr};
+    size_t out_cap[2] = {0, 0};
+    cudaEvent_t out_ready[2] = {nullptr, nullptr};
+    cudaEvent_t out_free[2] = {nullptr, nullptr};
     // one event per outstanding submission (after its output copies), oldest first; spare events
     std::deque<cudaEvent_t> inflight;
     std::vector<cudaEvent_t> spare_events;
@@ -72,14 +80,19 @@ struct rfdetr_context {
         if (engine) cudaSetDevice(engine->device());
         if (copy_stream) cudaStreamSynchronize(copy_stream);
         if (engine) cudaStreamSynchronize(engine->stream());
+        if (d2h_stream) cudaStreamSynchronize(d2h_stream);
         for (cudaEvent_t ev : inflight) cudaEventDestroy(ev);
         for (cudaEvent_t ev : spare_events) cudaEventDestroy(ev);
         for (int k = 0; k < 2; ++k) {
             if (d_slot[k]) cudaFree(d_slot[k]);
             if (slot_ready[k]) cudaEventDestroy(slot_ready[k]);
             if (slot_free[k]) cudaEventDestroy(slot_free[k]);
+            if (d_out[k]) cudaFree(d_out[k]);
+            if (out_ready[k]) cudaEventDestroy(out_ready[k]);
+            if (out_free[k]) cudaEventDestroy(out_free[k]);
         }
         if (copy_stream) cudaStreamDestroy(copy_stream);
+        if (d2h_stream) cudaStreamDestroy(d2h_stream);
         if (d_dets) cudaFree(d_dets);
         if (d_counts) cudaFree(d_counts);
         if (d_filter) cudaFree(d_filter);
@@ -458,11 +471,14 @@ extern "C" rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8
     rfdetr_status s = e.reserve(batch);  // synchronizes the engine stream before growing
     if (s != RFDETR_OK) return s;
     if (!ctx->copy_stream) {
-        if (RFB_CUDA_FAIL(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking)))
+        if (RFB_CUDA_FAIL(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking)) ||
+            RFB_CUDA_FAIL(cudaStreamCreateWithFlags(&ctx->d2h_stream, cudaStreamNonBlocking)))
             return RFDETR_ERR_INFERENCE;
         for (int k = 0; k < 2; ++k)
             if (RFB_CUDA_FAIL(cudaEventCreateWithFlags(&ctx->slot_ready[k], cudaEventDisableTiming)) ||
-                RFB_CUDA_FAIL(cudaEventCreateWithFlags(&ctx->slot_free[k], cudaEventDisableTiming)))
+                RFB_CUDA_FAIL(cudaEventCreateWithFlags(&ctx->slot_free[k], cudaEventDisableTiming)) ||
+                RFB_CUDA_FAIL(cudaEventCreateWithFlags(&ctx->out_ready[k], cudaEventDisableTiming)) ||
+                RFB_CUDA_FAIL(cudaEventCreateWithFlags(&ctx->out_free[k], cudaEventDisableTiming)))
                 return RFDETR_ERR_INFERENCE;
     }
     const int k = ctx->next_slot;
@@ -486,8 +502,32 @@ extern "C" rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8
     s = e.enqueue(batch, ctx->d_slot[k], width, height);
     if (s != RFDETR_OK) return s;
     if (RFB_CUDA_FAIL(cudaEventRecord(ctx->slot_free[k], e.stream()))) return RFDETR_ERR_INFERENCE;
-    s = enqueue_output_copies(ctx, batch, out_logits, out_boxes, out_masks);
-    if (s != RFDETR_OK) return s;
+    // outputs: device copy into output slot k behind the forward (once the slot's previous
+    // transfer is done), then the transfer to the caller on d2h_stream
+    const rfb::Config& c = e.cfg();
+    const size_t nq = c.num_queries, nc = c.num_classes, hw = (size_t)e.mask_side() * e.mask_side();
+    const size_t lb = out_logits ? (size_t)batch * nq * nc * 4 : 0, bb = out_boxes ? (size_t)batch * nq * 16 : 0;
+    const size_t mb = out_masks && c.has_seg ? (size_t)batch * nq * hw * 4 : 0;
+    if (lb + bb + mb > ctx->out_cap[k]) {
+        if (RFB_CUDA_FAIL(cudaEventSynchronize(ctx->out_free[k]))) return RFDETR_ERR_INFERENCE;
+        if (ctx->d_out[k]) cudaFree(ctx->d_out[k]);
+        ctx->d_out[k] = nullptr;
+        ctx->out_cap[k] = 0;
+        if (RFB_CUDA_FAIL(cudaMalloc(&ctx->d_out[k], lb + bb + mb))) return RFDETR_ERR_OUT_OF_MEMORY;
+        ctx->out_cap[k] = lb + bb + mb;
+    }
+    uint8_t* o = ctx->d_out[k];
+    const cudaStream_t es = e.stream(), ds = ctx->d2h_stream;
+    if (RFB_CUDA_FAIL(cudaStreamWaitEvent(es, ctx->out_free[k], 0)) ||
+        (lb && RFB_CUDA_FAIL(cudaMemcpyAsync(o, e.logits(), lb, cudaMemcpyDeviceToDevice, es))) ||
+        (bb && RFB_CUDA_FAIL(cudaMemcpyAsync(o + lb, e.boxes(), bb, cudaMemcpyDeviceToDevice, es))) ||
+        (mb && RFB_CUDA_FAIL(cudaMemcpyAsync(o + lb + bb, e.masks(), mb, cudaMemcpyDeviceToDevice, es))) ||
+        RFB_CUDA_FAIL(cudaEventRecord(ctx->out_ready[k], es)) || RFB_CUDA_FAIL(cudaStreamWaitEvent(ds, ctx->out_ready[k], 0)) ||
+        (lb && RFB_CUDA_FAIL(cudaMemcpyAsync(out_logits, o, lb, cudaMemcpyDeviceToHost, ds))) ||
+        (bb && RFB_CUDA_FAIL(cudaMemcpyAsync(out_boxes, o + lb, bb, cudaMemcpyDeviceToHost, ds))) ||
+        (mb && RFB_CUDA_FAIL(cudaMemcpyAsync(out_masks, o + lb + bb, mb, cudaMemcpyDeviceToHost, ds))) ||
+        RFB_CUDA_FAIL(cudaEventRecord(ctx->out_free[k], ds)))
+        return RFDETR_ERR_INFERENCE;
     cudaEvent_t done = nullptr;
     if (!ctx->spare_events.empty()) {
         done = ctx->spare_events.back();
@@ -495,7 +535,7 @@ extern "C" rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8
     } else if (RFB_CUDA_FAIL(cudaEventCreateWithFlags(&done, cudaEventDisableTiming))) {
         return RFDETR_ERR_INFERENCE;
     }
-    if (RFB_CUDA_FAIL(cudaEventRecord(done, e.stream()))) {
+    if (RFB_CUDA_FAIL(cudaEventRecord(done, ds))) {
         ctx->spare_events.push_back(done);
         return RFDETR_ERR_INFERENCE;
     }
@@ -522,7 +562,8 @@ extern "C" rfdetr_status rfdetr_b200_wait(rfdetr_context* ctx) {
     }
     if (ctx->copy_stream) {
         if (RFB_CUDA_FAIL(cudaSetDevice(ctx->engine->device())) ||
-            RFB_CUDA_FAIL(cudaStreamSynchronize(ctx->copy_stream)))
+            RFB_CUDA_FAIL(cudaStreamSynchronize(ctx->copy_stream)) ||
+            RFB_CUDA_FAIL(cudaStreamSynchronize(ctx->d2h_stream)))
             return RFDETR_ERR_INFERENCE;
     }
     return ctx->engine->finish();

@@ -180,10 +180,11 @@ def test_split_k_layernorm_gemms_match_the_oracle(make_model):
 
 def test_pipelined_submissions_match_forward_rgb(make_model):
     """rfdetr_b200_submit_rgb / rfdetr_b200_wait: several batches in flight
-    (uploads on a copy stream into two alternating device slots, forwards and
-    output copies on the engine stream) give, batch for batch, the outputs of
-    the synchronous rfdetr_b200_forward_rgb; a larger batch and another image
-    size in the middle of the stream regrow the slots."""
+    (uploads on a copy stream into two alternating device slots, forwards on
+    the engine stream, outputs copied into two alternating device slots and
+    downloaded on a third stream) give, batch for batch, the outputs of the
+    synchronous rfdetr_b200_forward_rgb; a larger batch and another image size
+    in the middle of the stream regrow the slots."""
     import torch
     from rfdetr_b200 import lib
 
@@ -203,6 +204,35 @@ def test_pipelined_submissions_match_forward_rgb(make_model):
     eng.wait()
     for (lg, bx), (wl, wb) in zip(outs, want):
         assert np.array_equal(lg.numpy(), wl) and np.array_equal(bx.numpy(), wb)
+    eng.close()
+
+
+def test_pipelined_submissions_with_masks(make_model):
+    """Segmentation outputs through rfdetr_b200_submit_rgb (logits, boxes and masks through the
+    device output slots and the download stream) equal rfdetr_b200_forward_rgb's, batch for
+    batch; a submission that asks for the logits only writes nothing else."""
+    import torch
+    from rfdetr_b200 import lib
+
+    path = make_model("seg-tiny", "f16", 0)
+    eng = lib.Engine(path, max_batch=2)
+    S, m = eng.image_size, eng.mask_side
+    assert m > 0
+    batches = [_images(S, 2, 61 + i) for i in range(4)]
+    want = [eng.forward_rgb(x) for x in batches]
+    outs = []
+    for x in batches:
+        o = (torch.empty((2, eng.nq, eng.nc)).pin_memory(), torch.empty((2, eng.nq, 4)).pin_memory(),
+             torch.empty((2, eng.nq, m, m)).pin_memory())
+        eng.submit_rgb(x, o[0].numpy(), o[1].numpy(), o[2].numpy())
+        outs.append(o)
+    only = torch.empty((2, eng.nq, eng.nc)).pin_memory()
+    eng.submit_rgb(batches[1], only.numpy(), None)
+    eng.wait()
+    for o, w in zip(outs, want):
+        for got, ref in zip(o, w):
+            assert np.array_equal(got.numpy(), ref)
+    assert np.array_equal(only.numpy(), want[1][0])
     eng.close()
 
 
