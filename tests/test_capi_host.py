@@ -87,6 +87,33 @@ def test_inspect_errors(tmp_path):
     assert lib.inspect(p)[0] == -6
 
 
+def test_inspect_survives_corrupted_files(tmp_path):
+    """The GGUF reader on damaged input (src/model_loader.cpp reads untrusted files): seeded byte
+    flips and 8-byte overwrites (string lengths, counts, offsets, types) in the header, metadata
+    and tensor-info region, and truncations at random offsets.  Every call returns OK or one of
+    the status codes; none may crash (the sanitize build of the Makefile runs this under ASan +
+    UBSan)."""
+    good = _write(tmp_path, "good.gguf", dtype="f16")
+    data = open(good, "rb").read()
+    head = min(len(data), 16384)
+    rng = np.random.default_rng(1234)
+    statuses = set(lib.STATUS)
+    p = str(tmp_path / "bad.gguf")
+    for i in range(90):
+        b = bytearray(data)
+        if i % 3 == 0:
+            b = b[: int(rng.integers(0, len(data)))]
+        elif i % 3 == 1:
+            for _ in range(int(rng.integers(1, 4))):
+                b[int(rng.integers(0, head))] ^= 1 << int(rng.integers(0, 8))
+        else:
+            at = int(rng.integers(0, head - 8))
+            b[at:at + 8] = rng.integers(0, 256, 8, dtype=np.uint8).tobytes()
+        open(p, "wb").write(bytes(b))
+        st, _ = lib.inspect(p)
+        assert st in statuses, (i, st)
+
+
 def test_inspect_rejects_unsupported_config(tmp_path):
     cfg = synth.get_variant("tiny")
     cfg["backbone"]["heads"] = 8  # head_dim 48: not implemented by the kernels
