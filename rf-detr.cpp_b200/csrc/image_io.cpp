@@ -60,10 +60,21 @@ bool decode_png(const uint8_t* d, size_t n, int* w, int* h, std::vector<uint8_t>
         case 6: chans = 4; break;
         default: return false;
     }
-    if (!(depth == 8 || depth == 16 || (depth < 8 && (ctype == 0 || ctype == 3)))) return false;
+    // the bit depths the PNG specification allows for each colour type: the
+    // sub-byte unpacking below relies on depth dividing 8
+    bool depth_ok = false;
+    switch (ctype) {
+        case 0: depth_ok = depth == 1 || depth == 2 || depth == 4 || depth == 8 || depth == 16; break;
+        case 3: depth_ok = depth == 1 || depth == 2 || depth == 4 || depth == 8; break;
+        default: depth_ok = depth == 8 || depth == 16; break;
+    }
+    if (!depth_ok) return false;
     const size_t bpp_bits = (size_t)chans * depth;
     const size_t stride = (W * bpp_bits + 7) / 8;
     const size_t bpp = (bpp_bits + 7) / 8;
+    // deflate expands its input at most 1032:1, so an image larger than that
+    // bound of the IDAT bytes is corrupt: rejected before its buffers exist
+    if ((stride + 1) * H > idat.size() * 1032 + 1024) return false;
     std::vector<uint8_t> raw((stride + 1) * H);
     uLongf rawlen = (uLongf)raw.size();
     if (uncompress(raw.data(), &rawlen, idat.data(), (uLong)idat.size()) != Z_OK || rawlen != raw.size()) return false;

@@ -188,6 +188,74 @@ def test_png_and_ppm_decode(filt):
     assert st.value == -2
 
 
+def _png_chunks(w, h, depth, ctype, rows):
+    def chunk(t, d):
+        return struct.pack(">I", len(d)) + t + d + struct.pack(">I", zlib.crc32(t + d) & 0xFFFFFFFF)
+    return (b"\x89PNG\r\n\x1a\n" + chunk(b"IHDR", struct.pack(">IIBBBBB", w, h, depth, ctype, 0, 0, 0)) +
+            chunk(b"IDAT", zlib.compress(rows)) + chunk(b"IEND", b""))
+
+
+def test_png_bit_depths():
+    """Gray PNGs of the specification's sub-byte depths (1, 2, 4) decode to the expected levels;
+    depths 3, 5, 6 and 7 (not in the specification) are RFDETR_ERR_DECODE, not unpacked past the
+    end of each row."""
+    L = lib.lib()
+    W, H = 100, 2
+    rng = np.random.default_rng(8)
+    for depth in range(1, 8):
+        stride = (W * depth + 7) // 8
+        raw = rng.integers(0, 256, (H, stride), dtype=np.uint8)
+        blob = _png_chunks(W, H, depth, 0, b"".join(b"\x00" + raw[y].tobytes() for y in range(H)))
+        st = C.c_int(0)
+        img = L.rfdetr_image_load_buffer(blob, len(blob), C.byref(st))
+        if depth in (1, 2, 4):
+            assert img and st.value == 0
+            got = np.ctypeslib.as_array(L.rfdetr_image_rgb_data(img), shape=(H * W * 3,)).reshape(H, W, 3)
+            bits = np.unpackbits(raw, axis=1)[:, : W * depth].reshape(H, W, depth)
+            level = (bits * (1 << np.arange(depth - 1, -1, -1))).sum(-1)
+            assert np.array_equal(got[..., 0], level * 255 // ((1 << depth) - 1))
+            L.rfdetr_image_free(img)
+        else:
+            assert not img and st.value == -5, depth
+
+
+def test_png_rejects_sizes_its_data_cannot_hold():
+    """An IHDR of 65535 x 65535 16-bit RGBA pixels over a few bytes of IDAT is RFDETR_ERR_DECODE
+    at once: deflate expands at most 1032:1, so no buffer of the declared size is allocated."""
+    L = lib.lib()
+    blob = _png_chunks(65535, 65535, 16, 6, bytes(64))
+    st = C.c_int(0)
+    assert not L.rfdetr_image_load_buffer(blob, len(blob), C.byref(st)) and st.value == -5
+
+
+def test_image_decoders_survive_corrupted_input():
+    """PNG (two filters) and PPM decoding of damaged buffers: seeded byte flips, 4-byte overwrites
+    (chunk lengths, dimensions, header numbers) and truncations give an image whose pixel buffer
+    matches its dimensions, or RFDETR_ERR_DECODE; none may crash (clean under the sanitize build)."""
+    L = lib.lib()
+    rgb = np.random.default_rng(9).integers(0, 256, (17, 23, 3), dtype=np.uint8)
+    rng = np.random.default_rng(4321)
+    for blob in (_png(rgb), _png(rgb, filt=1), b"P6\n23 17\n255\n" + rgb.tobytes()):
+        for i in range(120):
+            b = bytearray(blob)
+            if i % 3 == 0:
+                b = b[: int(rng.integers(1, len(blob)))]
+            elif i % 3 == 1:
+                for _ in range(int(rng.integers(1, 4))):
+                    b[int(rng.integers(0, min(len(b), 64)))] ^= 1 << int(rng.integers(0, 8))
+            else:
+                at = int(rng.integers(0, min(len(b), 64) - 4))
+                b[at:at + 4] = rng.integers(0, 256, 4, dtype=np.uint8).tobytes()
+            st = C.c_int(0)
+            img = L.rfdetr_image_load_buffer(bytes(b), len(b), C.byref(st))
+            if img:
+                w, h = L.rfdetr_image_width(img), L.rfdetr_image_height(img)
+                assert st.value == 0 and w > 0 and h > 0
+                L.rfdetr_image_free(img)
+            else:
+                assert st.value == -5, (i, st.value)
+
+
 def test_image_from_rgb_copies():
     L = lib.lib()
     rgb = np.arange(4 * 5 * 3, dtype=np.uint8).reshape(4, 5, 3)
