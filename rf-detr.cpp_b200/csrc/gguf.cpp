@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <new>
 
 namespace rfb {
 
@@ -18,7 +19,12 @@ enum : uint32_t {
 
 struct Reader {
     FILE* f;
+    uint64_t size = 0;  // file size: no length read from the file may exceed what is left of it
     bool ok = true;
+    uint64_t left() const {
+        const long p = std::ftell(f);
+        return p < 0 || (uint64_t)p > size ? 0 : size - (uint64_t)p;
+    }
     template <class T>
     T get() {
         T v{};
@@ -27,7 +33,7 @@ struct Reader {
     }
     std::string str() {
         const uint64_t n = get<uint64_t>();
-        if (!ok || n > (1ull << 30)) { ok = false; return {}; }
+        if (!ok || n > left()) { ok = false; return {}; }
         std::string s(n, '\0');
         if (n && std::fread(&s[0], 1, n, f) != n) ok = false;
         return s;
@@ -113,11 +119,17 @@ bool ggml_type_block(uint32_t t, size_t* bb, int* be) {
     }
 }
 
-int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
+namespace {
+
+int gguf_read_impl(const std::string& path, GgufFile* out, std::string* err) {
     auto fail = [&](int code, const char* m) { if (err) *err = m; return code; };
     std::unique_ptr<FILE, int (*)(FILE*)> fp(std::fopen(path.c_str(), "rb"), &std::fclose);
     if (!fp) return fail(-2, "file not found");
     Reader r{fp.get()};
+    if (std::fseek(r.f, 0, SEEK_END) != 0) return fail(-3, "seek failed");
+    const long fsize = std::ftell(r.f);
+    if (fsize < 0 || std::fseek(r.f, 0, SEEK_SET) != 0) return fail(-3, "seek failed");
+    r.size = (uint64_t)fsize;
     char magic[4];
     if (std::fread(magic, 1, 4, r.f) != 4 || std::memcmp(magic, "GGUF", 4) != 0) return fail(-6, "bad GGUF magic");
     out->version = r.get<uint32_t>();
@@ -137,7 +149,9 @@ int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
         } else if (v.type == V_ARR) {
             v.arr_type = r.get<uint32_t>();
             const uint64_t n = r.get<uint64_t>();
-            if (!r.ok || n > (1ull << 26)) return fail(-6, "corrupt GGUF array");
+            // every element takes at least one byte of the file (a string at least its 8-byte length)
+            const uint64_t min_elem = v.arr_type == V_STR ? 8 : (scalar_size(v.arr_type) ? scalar_size(v.arr_type) : 1);
+            if (!r.ok || n > r.left() / min_elem) return fail(-6, "corrupt GGUF array");
             if (v.arr_type == V_STR) {
                 v.strs.reserve(n);
                 for (uint64_t j = 0; j < n && r.ok; ++j) v.strs.push_back(r.str());
@@ -175,7 +189,14 @@ int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
         t.name = r.str();
         t.n_dims = (int)r.get<uint32_t>();
         if (!r.ok || t.n_dims < 1 || t.n_dims > 4) return fail(-6, "corrupt GGUF tensor info");
-        for (int d = 0; d < t.n_dims; ++d) t.ne[d] = (int64_t)r.get<uint64_t>();
+        uint64_t elems = 1;
+        for (int d = 0; d < t.n_dims; ++d) {
+            const uint64_t n = r.get<uint64_t>();
+            if (n >= (1ull << 32)) return fail(-6, "corrupt GGUF tensor shape");
+            t.ne[d] = (int64_t)n;
+            elems *= n;  // < 2^48 after each step: no overflow
+            if (elems >= (1ull << 48)) return fail(-6, "corrupt GGUF tensor shape");
+        }
         t.type = r.get<uint32_t>();
         t.offset = r.get<uint64_t>();
         if (!r.ok) return fail(-6, "truncated GGUF tensor info");
@@ -189,6 +210,7 @@ int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
     uint64_t align = 32;
     auto ita = out->kv.find("general.alignment");
     if (ita != out->kv.end()) align = ita->second.u ? ita->second.u : 32;
+    if (align > (1u << 20) || (align & (align - 1))) return fail(-6, "corrupt GGUF alignment");
     out->alignment = align;
     long pos = std::ftell(r.f);
     if (pos < 0) return fail(-3, "ftell failed");
@@ -198,11 +220,23 @@ int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
     if (end < 0 || (uint64_t)end < data_start) return fail(-6, "GGUF data section missing");
     const uint64_t data_size = (uint64_t)end - data_start;
     for (const auto& t : out->tensors)
-        if (t.offset + t.nbytes > data_size) return fail(-6, "tensor data out of file bounds (truncated file?)");
+        if (t.offset > data_size || t.nbytes > data_size - t.offset)
+            return fail(-6, "tensor data out of file bounds (truncated file?)");
     out->data.resize(data_size);
     if (std::fseek(r.f, (long)data_start, SEEK_SET) != 0) return fail(-3, "seek failed");
     if (data_size && std::fread(out->data.data(), 1, data_size, r.f) != data_size) return fail(-3, "read failed");
     return 0;
+}
+
+}  // namespace
+
+int gguf_read(const std::string& path, GgufFile* out, std::string* err) {
+    try {
+        return gguf_read_impl(path, out, err);
+    } catch (const std::bad_alloc&) {
+        if (err) *err = "out of memory reading the GGUF file";
+        return -4;
+    }
 }
 
 int gguf_write(const std::string& path, const GgufFile& f, std::string* err) {

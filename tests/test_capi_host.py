@@ -114,6 +114,38 @@ def test_inspect_survives_corrupted_files(tmp_path):
         assert st in statuses, (i, st)
 
 
+def test_gguf_reader_checks_lengths_against_the_file(tmp_path):
+    """Lengths and offsets read from a GGUF file are checked against the file itself: a tensor
+    offset near 2^64 (whose end would wrap around past the bounds check) is rejected, and so are
+    a metadata string length and an array count larger than the bytes left in the file, before
+    anything is allocated for them."""
+    good = _write(tmp_path, "good.gguf", dtype="f16")
+    data = bytes(open(good, "rb").read())
+    assert lib.inspect(good)[0] == 0
+
+    def status(b):
+        p = tmp_path / "bad.gguf"
+        p.write_bytes(bytes(b))
+        return lib.inspect(str(p))[0]
+
+    name = b"decoder.layers.1.norm3.bias"
+    at = data.find(struct.pack("<Q", len(name)) + name)
+    assert at > 0
+    n_dims = struct.unpack_from("<I", data, at + 8 + len(name))[0]
+    b = bytearray(data)
+    struct.pack_into("<Q", b, at + 8 + len(name) + 4 + 8 * n_dims + 4, 2**64 - 16)  # the tensor's offset
+    assert status(b) == -6
+    b = bytearray(data)
+    struct.pack_into("<Q", b, 24, (1 << 30) - 1)  # length of the first metadata key
+    assert status(b) == -6
+    key = b"rfdetr.class_names"
+    at = data.find(struct.pack("<Q", len(key)) + key)
+    assert at > 0
+    b = bytearray(data)
+    struct.pack_into("<Q", b, at + 8 + len(key) + 8, 1 << 25)  # element count of the string array
+    assert status(b) == -6
+
+
 def test_inspect_rejects_unsupported_config(tmp_path):
     cfg = synth.get_variant("tiny")
     cfg["backbone"]["heads"] = 8  # head_dim 48: not implemented by the kernels
