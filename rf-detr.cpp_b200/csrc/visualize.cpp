@@ -8,6 +8,7 @@
 #include "image_io.hpp"
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 
 namespace {
@@ -29,12 +30,16 @@ void fill(rfdetr_image* img, int x0, int y0, int x1, int y1, const uint8_t* c) {
         }
 }
 
+// Pixel coordinate of a caller's box edge: NaN draws at 0 and values are held
+// to +-1e6, so the conversion and the edge arithmetic below cannot overflow.
+int coord(float v) { return std::isnan(v) ? 0 : (int)std::clamp(v, -1.0e6f, 1.0e6f); }
+
 }  // namespace
 
 extern "C" void rfdetr_visualize_draw_box(rfdetr_image* img, rfdetr_detection det, int thickness) {
     if (!img || img->rgb.empty()) return;
     const uint8_t* c = kPalette[det.class_id % 20];
-    const int x0 = (int)det.x1, y0 = (int)det.y1, x1 = (int)det.x2, y1 = (int)det.y2;
+    const int x0 = coord(det.x1), y0 = coord(det.y1), x1 = coord(det.x2), y1 = coord(det.y2);
     int t = std::max(thickness, 3);
     t = std::min(t, std::max(1, std::min(x1 - x0, y1 - y0) / 2));
     fill(img, x0, y0, x1, y0 + t, c);
@@ -59,7 +64,7 @@ extern "C" void rfdetr_visualize_overlay_mask(rfdetr_image* img, rfdetr_detectio
 
 extern "C" rfdetr_status rfdetr_render(const rfdetr_image* img, const rfdetr_detection* dets, size_t n,
                                        const char* out_path) {
-    if (!img || !out_path || img->rgb.empty()) return RFDETR_ERR_INVALID_ARG;
+    if (!img || !out_path || img->rgb.empty() || (n && !dets)) return RFDETR_ERR_INVALID_ARG;
     rfdetr_image copy = *img;
     for (size_t i = 0; i < n; ++i) rfdetr_visualize_overlay_mask(&copy, dets[i], 0.45f);
     for (size_t i = 0; i < n; ++i) rfdetr_visualize_draw_box(&copy, dets[i], 3);

@@ -300,6 +300,34 @@ def test_image_from_rgb_copies():
     assert not L.rfdetr_image_from_rgb_buffer(None, 5, 4, C.byref(st)) and st.value == -1
 
 
+def test_visualize_any_box(tmp_path):
+    """rfdetr_visualize_draw_box with caller boxes outside the image, inverted, NaN or infinite
+    writes inside the image only; a sane box gets its edges in the class colour and keeps its
+    interior; rfdetr_render rejects a NULL detection array with n > 0."""
+    L = lib.lib()
+    rgb = np.zeros((40, 50, 3), np.uint8)
+    st = C.c_int(0)
+    img = L.rfdetr_image_from_rgb_buffer(rgb.ctypes.data, 50, 40, C.byref(st))
+    d = lib.Detection()
+    d.class_id = 1
+    inf, nan = float("inf"), float("nan")
+    for box in [(-100, -100, 1e9, 1e9), (30, 20, 5, 5), (nan, nan, nan, nan), (-inf, 0, inf, 40),
+                (1e30, -1e30, 3, 3), (49.9, 39.9, 60, 60)]:
+        d.x1, d.y1, d.x2, d.y2 = box
+        L.rfdetr_visualize_draw_box(img, d, 3)
+        L.rfdetr_visualize_draw_box(img, d, -7)
+    L.rfdetr_image_free(img)
+    img = L.rfdetr_image_from_rgb_buffer(rgb.ctypes.data, 50, 40, C.byref(st))
+    d.x1, d.y1, d.x2, d.y2 = 5, 18, 30, 35
+    L.rfdetr_visualize_draw_box(img, d, 3)
+    px = np.ctypeslib.as_array(L.rfdetr_image_rgb_data(img), shape=(40 * 50 * 3,)).reshape(40, 50, 3)
+    assert px[18, 5].tolist() == [60, 180, 75] and px[34, 29].tolist() == [60, 180, 75]
+    assert px[26, 17].tolist() == [0, 0, 0]
+    assert L.rfdetr_render(img, None, 2, str(tmp_path / "r.png").encode()) == -1
+    assert L.rfdetr_render(img, None, 0, str(tmp_path / "r.png").encode()) == 0
+    L.rfdetr_image_free(img)
+
+
 def test_flat_capi_invalid_handles():
     L = lib.lib()
     assert L.rfdetr_capi_unload(0) == 0
