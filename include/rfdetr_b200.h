@@ -183,6 +183,17 @@ int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes, int batch
                           int top_k, const uint32_t* d_class_filter, int filter_len, int img_w, int img_h,
                           rfdetr_b200_det* d_out, int* d_counts, void* stream);
 
+/* The legacy preprocess resize (src/image_io.cpp:249-275: models whose
+ * rfdetr.preprocess.resize_mode is legacy_stb or absent resize images that are
+ * not at the model size with stb_image_resize2's stbir_resize_uint8_linear):
+ * d_src uint8 HWC [batch][h][w][3] -> d_dst uint8 HWC [batch][oh][ow][3],
+ * Catmull-Rom for a growing axis, Mitchell for a shrinking one, a copy for an
+ * axis that keeps its size, clamped edges.  Outputs equal the library's except
+ * for a byte differing by one where a value lies within float rounding of a
+ * half.  Synchronizes `stream` before returning.  Device pointers. */
+int rfdetr_b200_op_resize_legacy(const uint8_t* d_src, int batch, int w, int h, uint8_t* d_dst, int ow, int oh,
+                                 void* stream);
+
 /* Two-stage query selection (src/rfdetr_model.cpp:39-62, top_k_by_max_class):
  * for each image b, the k of its n tokens with the largest maximum class logit
  * (d_cls f32 [batch][n][nc]), in descending order of that maximum (ties: lower

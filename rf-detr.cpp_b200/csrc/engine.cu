@@ -47,6 +47,7 @@ Engine::~Engine() {
     drop_graphs();
     free_activations();
     if (rgb_u8_) cudaFree(rgb_u8_);
+    for (auto& l : legacy_) cudaFree(l.taps.base);
     for (void* p : wallocs_) cudaFree(p);
     if (d_err_) cudaFree(d_err_);
     for (cudaEvent_t e : prof_ev_) cudaEventDestroy(e);
@@ -451,6 +452,8 @@ rfdetr_status Engine::alloc_activations(int B) {
         {(void**)&bdelta_, Mq * 4 * 4},
         {(void**)&boxes_, Mq * 4 * 4},
     };
+    rsz_ = nullptr;
+    if (!cfg_.bilinear_no_antialias) reqs.push_back({(void**)&rsz_, (size_t)B * S_ * S_ * 3});
     if (cfg_.has_seg) {
         reqs.push_back({(void**)&sp32_, (size_t)B * HW * Dm_ * 4});
         reqs.push_back({(void**)&sln16_, (size_t)B * HW * Dm_ * 2});
@@ -552,7 +555,29 @@ void Engine::drop_graphs() {
     graphs_.clear();
 }
 
+rfdetr_status Engine::prepare_legacy(int w, int h) {
+    if (legacy_taps(w, h)) return RFDETR_OK;
+    if (RFB_CUDA_FAIL(cudaSetDevice(device_))) return RFDETR_ERR_INFERENCE;
+    LegacyEntry e{w, h, {}};
+    const cudaError_t ce = upload_legacy_taps(w, h, S_, S_, &e.taps);
+    if (ce == cudaErrorMemoryAllocation) return RFDETR_ERR_OUT_OF_MEMORY;
+    if (RFB_CUDA_FAIL(ce)) return RFDETR_ERR_INFERENCE;
+    legacy_.push_back(e);
+    return RFDETR_OK;
+}
+
+const LegacyTapsDev* Engine::legacy_taps(int w, int h) const {
+    for (const auto& l : legacy_)
+        if (l.w == w && l.h == h) return &l.taps;
+    return nullptr;
+}
+
 rfdetr_status Engine::enqueue(int B, const uint8_t* src_rgb, int src_w, int src_h) {
+    if (src_rgb && legacy_resize(src_w, src_h)) {
+        // taps are uploaded here, before any capture, so that replays reuse them
+        const rfdetr_status s = prepare_legacy(src_w, src_h);
+        if (s != RFDETR_OK) return s;
+    }
     if (!use_graphs_ || profiling_) return enqueue_raw(B, src_rgb, src_w, src_h);
     if (RFB_CUDA_FAIL(cudaSetDevice(device_))) return RFDETR_ERR_INFERENCE;
     for (auto& g : graphs_) {
@@ -619,7 +644,17 @@ rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int 
     // ---- preprocess + patch im2col in windowed order (one kernel from uint8)
     if (src_rgb) {
         if (src_w <= 0 || src_h <= 0) return RFDETR_ERR_INVALID_ARG;
-        L.check(patch_from_rgb(src_rgb, B, src_w, src_h, S_, P_, nw_, Kpad_, cfg_.mean, cfg_.std, apatch_, st),
+        const uint8_t* pix = src_rgb;
+        int pw = src_w, ph = src_h;
+        if (legacy_resize(src_w, src_h)) {
+            // legacy_stb models: the library resize to S x S (uint8), then the identity path
+            const LegacyTapsDev* t = legacy_taps(src_w, src_h);
+            if (!t || !rsz_) return RFDETR_ERR_INFERENCE;
+            L.check(resize_legacy_rgb(src_rgb, B, src_w, src_h, *t, S_, S_, rsz_, st), "resize_legacy");
+            pix = rsz_;
+            pw = ph = S_;
+        }
+        L.check(patch_from_rgb(pix, B, pw, ph, S_, P_, nw_, Kpad_, cfg_.mean, cfg_.std, apatch_, st),
                 "patch_from_rgb");
     } else {
         L.check(patch_im2col(img_, B, S_, P_, nw_, Kpad_, apatch_, st), "patch_im2col");

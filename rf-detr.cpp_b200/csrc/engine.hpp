@@ -6,6 +6,7 @@
 #pragma once
 
 #include "model.hpp"
+#include "resize_legacy.hpp"
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -98,6 +99,17 @@ private:
     };
     std::vector<GraphEntry> graphs_;
     bool use_graphs_ = true;
+    // Legacy preprocess resize (resize_mode legacy_stb): taps per source size,
+    // uploaded outside any graph capture and kept for the engine's lifetime;
+    // the resized batch goes through rsz_ [max_batch][S][S][3].
+    struct LegacyEntry {
+        int w, h;
+        LegacyTapsDev taps;
+    };
+    std::vector<LegacyEntry> legacy_;
+    bool legacy_resize(int w, int h) const { return !cfg_.bilinear_no_antialias && (w != S_ || h != S_); }
+    rfdetr_status prepare_legacy(int w, int h);
+    const LegacyTapsDev* legacy_taps(int w, int h) const;
     rfdetr_status upload_weights(const Model& m);
     rfdetr_status alloc_activations(int batch);
     void free_activations();
@@ -168,6 +180,7 @@ private:
     int* d_err_ = nullptr;
     uint8_t* rgb_u8_ = nullptr;
     size_t rgb_cap_ = 0;
+    uint8_t* rsz_ = nullptr;
     float* img_ = nullptr;
     __half* apatch_ = nullptr;
     float* x_ = nullptr;

@@ -66,6 +66,45 @@ __global__ void k_preprocess(const uint8_t* __restrict__ rgb, int B, int w, int 
     }
 }
 
+// ---- legacy preprocess resize: src/image_io.cpp:249-275 (taps: resize_legacy.cpp)
+// One thread per output pixel: for each vertical tap, the horizontal weighted
+// sum of the row's taps, then the weighted sum of those rows, in tap order with
+// a rounding after every multiply and every add (as the library's float
+// passes, horizontal first); the 0..255 result rounds half up and saturates.
+__global__ void k_resize_legacy(const uint8_t* __restrict__ src, int B, int w, int h, const int* __restrict__ xf,
+                                const int* __restrict__ xn, const float* __restrict__ xc, int xw,
+                                const int* __restrict__ yf, const int* __restrict__ yn,
+                                const float* __restrict__ yc, int yw, int ow, int oh, uint8_t* __restrict__ dst) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)B * oh * ow) return;
+    const int ox = (int)(i % ow);
+    const size_t r = i / ow;
+    const int oy = (int)(r % oh), b = (int)(r / oh);
+    const uint8_t* img = src + (size_t)b * h * w * 3;
+    const int x0 = xf[ox], nx = xn[ox], y0 = yf[oy], ny = yn[oy];
+    const float* cx = xc + (size_t)ox * xw;
+    const float* cy = yc + (size_t)oy * yw;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+    for (int j = 0; j < ny; ++j) {
+        const uint8_t* row = img + ((size_t)(y0 + j) * w + x0) * 3;
+        float h0 = 0.f, h1 = 0.f, h2 = 0.f;
+        for (int k = 0; k < nx; ++k) {
+            const float c = cx[k];
+            h0 = __fadd_rn(h0, __fmul_rn(c, (float)row[3 * k]));
+            h1 = __fadd_rn(h1, __fmul_rn(c, (float)row[3 * k + 1]));
+            h2 = __fadd_rn(h2, __fmul_rn(c, (float)row[3 * k + 2]));
+        }
+        const float c = cy[j];
+        a0 = __fadd_rn(a0, __fmul_rn(c, h0));
+        a1 = __fadd_rn(a1, __fmul_rn(c, h1));
+        a2 = __fadd_rn(a2, __fmul_rn(c, h2));
+    }
+    uint8_t* o = dst + i * 3;
+    const float a[3] = {a0, a1, a2};
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) o[ch] = (uint8_t)min(max(__float2int_rz(__fadd_rn(a[ch], 0.5f)), 0), 255);
+}
+
 // ---- patch im2col in windowed order: src/dinov2.cpp:339-408 -----------------
 __global__ void k_patch_im2col(const float* __restrict__ img, int B, int S, int p, int nw, int Kpad,
                                __half* __restrict__ A) {
@@ -997,6 +1036,16 @@ cudaError_t im2col3x3(const __half* src, int lds, int B, int H, int W, int C, __
 cudaError_t mask_memory(const float* mem, int B, int G, int C, __half* out, cudaStream_t st) {
     const size_t n = (size_t)B * G * G * C;
     k_mask_memory<<<cdiv(n, 256), 256, 0, st>>>(mem, B, G, C, out);
+    return cudaGetLastError();
+}
+
+cudaError_t resize_legacy_rgb(const uint8_t* src, int B, int w, int h, const LegacyTapsDev& t, int ow, int oh,
+                              uint8_t* dst, cudaStream_t st) {
+    if (!src || !dst || !t.base || B < 0 || w <= 0 || h <= 0 || ow <= 0 || oh <= 0) return cudaErrorInvalidValue;
+    if (B == 0) return cudaSuccess;
+    const size_t n = (size_t)B * ow * oh;
+    k_resize_legacy<<<cdiv(n, 256), 256, 0, st>>>(src, B, w, h, t.xf, t.xn, t.xc, t.xw, t.yf, t.yn, t.yc, t.yw, ow,
+                                                  oh, dst);
     return cudaGetLastError();
 }
 

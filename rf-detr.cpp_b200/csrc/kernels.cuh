@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "resize_legacy.hpp"
+
 namespace rfb {
 
 // Fused attention: O = softmax(scale * Q K^T) V per (group, head).  Q/K/V rows
@@ -28,6 +30,12 @@ cudaError_t preprocess_u8(const uint8_t* rgb, int B, int w, int h, int S, const 
 // Patch im2col in windowed order: planar [B][3][S][S] -> A [B*NW*Tp][Kpad] f16,
 // K ordered (channel, ky, kx), zero padded to Kpad.
 cudaError_t patch_im2col(const float* img, int B, int S, int p, int nw, int Kpad, __half* A, cudaStream_t st);
+
+// The legacy preprocess resize (rfdetr.preprocess.resize_mode = legacy_stb):
+// uint8 HWC [B][h][w][3] -> uint8 HWC [B][oh][ow][3] with the taps `t` of that
+// size pair (resize_legacy.hpp).
+cudaError_t resize_legacy_rgb(const uint8_t* src, int B, int w, int h, const LegacyTapsDev& t, int ow, int oh,
+                              uint8_t* dst, cudaStream_t st);
 
 // Preprocess fused with the patch im2col: uint8 HWC [B][h][w][3] -> A as above.
 cudaError_t patch_from_rgb(const uint8_t* rgb, int B, int w, int h, int S, int p, int nw, int Kpad,

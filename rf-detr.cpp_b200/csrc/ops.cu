@@ -57,6 +57,19 @@ extern "C" int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes
                                               static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int rfdetr_b200_op_resize_legacy(const uint8_t* d_src, int batch, int w, int h, uint8_t* d_dst, int ow,
+                                           int oh, void* stream) {
+    if (!d_src || !d_dst || batch < 0 || w <= 0 || h <= 0 || ow <= 0 || oh <= 0) return (int)cudaErrorInvalidValue;
+    rfb::LegacyTapsDev t;
+    cudaError_t e = rfb::upload_legacy_taps(w, h, ow, oh, &t);
+    if (e != cudaSuccess) return (int)e;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    e = rfb::resize_legacy_rgb(d_src, batch, w, h, t, ow, oh, d_dst, st);
+    const cudaError_t es = cudaStreamSynchronize(st);  // the taps are freed below
+    cudaFree(t.base);
+    return (int)(e != cudaSuccess ? e : es);
+}
+
 extern "C" int rfdetr_b200_op_topk(const float* d_cls, int batch, int n, int nc, int k, int32_t* d_idx,
                                    void* stream) {
     return (int)rfb::topk_tokens(d_cls, batch, n, nc, k, d_idx, static_cast<cudaStream_t>(stream));

@@ -125,6 +125,8 @@ SIGNATURES = {
                                            C.c_void_p]),
     "rfdetr_b200_quantize_gguf": (C.c_int, [C.c_char_p, C.c_char_p, C.c_int, C.c_int]),
     "rfdetr_b200_op_quantize": (C.c_int, [C.c_int, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
+    "rfdetr_b200_op_resize_legacy": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int,
+                                               C.c_void_p]),
     "rfdetr_b200_op_topk": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "rfdetr_b200_op_select": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
                                         C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),

@@ -331,3 +331,30 @@ def test_topk_by_max_class(B, N, NC, K):
     # sizes the kernel does not take are rejected before any launch
     assert L.rfdetr_b200_op_topk(_p(d_cls), B, 4097, NC, K, _p(d_idx), _stream()) != 0
     assert L.rfdetr_b200_op_topk(_p(d_cls), B, N, NC, N + 1, _p(d_idx), _stream()) != 0
+
+
+def test_resize_legacy_matches_the_reference_resize():
+    """The legacy preprocess resize (rfdetr_b200_op_resize_legacy) against the reference's own
+    stb_image_resize2 output (tests/golden/stb_resize.npz, pinned by
+    tests/test_stb_resize_golden.py): growing, shrinking, mixed, kept and 2:1 axes, a batch of two.
+    Bytes differ by at most one, and only where a value lies within float rounding of a half (the
+    library's SIMD sums run in another order): at least 99.9 % are identical."""
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import gen_stb_resize_golden as gen
+
+    golden = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "stb_resize.npz"))
+    L = _lib()
+    for seed, w, h, ow, oh in gen.CASES:
+        img = gen.source(seed, w, h)
+        src = torch.from_numpy(np.stack([img, img])).cuda()
+        dst = torch.zeros((2, oh, ow, 3), dtype=torch.uint8, device="cuda:0")
+        assert L.rfdetr_b200_op_resize_legacy(_p(src), 2, w, h, _p(dst), ow, oh, _stream()) == 0
+        got = dst.cpu().numpy().astype(np.int32)
+        want = golden[f"case_{seed}"].astype(np.int32)
+        for b in range(2):
+            d = np.abs(got[b] - want)
+            assert d.max() <= 1 and (d == 0).mean() >= 0.999, (seed, d.max(), (d == 0).mean())
+    assert L.rfdetr_b200_op_resize_legacy(None, 1, 4, 4, None, 2, 2, _stream()) != 0

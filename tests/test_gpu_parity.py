@@ -444,6 +444,40 @@ def test_detect_batch_matches_per_run_forwards(make_model):
     eng.close()
 
 
+def test_legacy_resize_mode(tmp_path):
+    """A model whose rfdetr.preprocess.resize_mode is legacy_stb resizes images that are not at the
+    model size with the library's resize (src/image_io.cpp:249-275): its forward of a 200 x 160
+    image equals, bit for bit, its forward of that image resized by rfdetr_b200_op_resize_legacy,
+    and differs from the 1.9 bilinear model's; at the model size both modes are the identity."""
+    import torch
+    from rfdetr_b200 import lib, synth
+
+    paths = {}
+    for mode in ("legacy_stb", "bilinear_no_antialias"):
+        cfg = synth.get_variant("tiny")
+        cfg["resize_mode"] = mode
+        paths[mode] = str(tmp_path / f"{mode}.gguf")
+        synth.write_gguf(paths[mode], "tiny", cfg, synth.make_state(synth.get_variant("tiny"), 0), "f16")
+    legacy = lib.Engine(paths["legacy_stb"], max_batch=2)
+    bilinear = lib.Engine(paths["bilinear_no_antialias"], max_batch=2)
+    S = legacy.image_size
+    img = np.random.default_rng(77).integers(0, 256, (2, 160, 200, 3), dtype=np.uint8)
+    lg, bx, _ = legacy.forward_rgb(img)
+    src = torch.from_numpy(img).cuda()
+    dst = torch.zeros((2, S, S, 3), dtype=torch.uint8, device="cuda:0")
+    L = lib.lib()
+    assert L.rfdetr_b200_op_resize_legacy(src.data_ptr(), 2, 200, 160, dst.data_ptr(), S, S,
+                                          torch.cuda.current_stream().cuda_stream) == 0
+    lg2, bx2, _ = legacy.forward_rgb(dst.cpu().numpy())
+    assert np.array_equal(lg, lg2) and np.array_equal(bx, bx2)
+    lg3, _, _ = bilinear.forward_rgb(img)
+    assert not np.array_equal(lg, lg3)
+    same = _images(S, 2, 78)
+    assert np.array_equal(legacy.forward_rgb(same)[0], bilinear.forward_rgb(same)[0])
+    legacy.close()
+    bilinear.close()
+
+
 def test_flat_capi_with_png_and_seg_masks(make_model, tmp_path):
     """LocalAI's flat API (rfdetr_capi_*) on a segmentation model: JSON
     envelope, accessors, two-call sizing, PNG masks at the image size, and
