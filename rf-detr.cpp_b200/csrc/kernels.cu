@@ -32,40 +32,6 @@ __device__ __forceinline__ int div_small(int x, float inv_d) {
     return __float2int_rz(__fmul_rn((float)x + 0.5f, inv_d));
 }
 
-// ---- preprocess: src/image_io.cpp:207-248 ----------------------------------
-__global__ void k_preprocess(const uint8_t* __restrict__ rgb, int B, int w, int h, int S, float m0, float m1,
-                             float m2, float s0, float s1, float s2, float* __restrict__ out) {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const size_t total = (size_t)B * S * S;
-    if (i >= total) return;
-    const int b = (int)(i / ((size_t)S * S));
-    const int r = (int)(i - (size_t)b * S * S);
-    const int yy = r / S, xx = r - (r / S) * S;
-    const double scx = (double)w / (double)S, scy = (double)h / (double)S;
-    const double fy = ((double)yy + 0.5) * scy - 0.5;
-    const int y0r = (int)floor(fy);
-    const int y0 = min(max(y0r, 0), h - 1), y1 = min(max(y0r + 1, 0), h - 1);
-    const float wy = (float)(fy - (double)y0r);
-    const double fx = ((double)xx + 0.5) * scx - 0.5;
-    const int x0r = (int)floor(fx);
-    const int x0 = min(max(x0r, 0), w - 1), x1 = min(max(x0r + 1, 0), w - 1);
-    const float wx = (float)(fx - (double)x0r);
-    const uint8_t* img = rgb + (size_t)b * h * w * 3;
-    const float mean[3] = {m0, m1, m2}, sd[3] = {s0, s1, s2};
-#pragma unroll
-    for (int c = 0; c < 3; ++c) {
-        const float p00 = (float)img[((size_t)y0 * w + x0) * 3 + c];
-        const float p01 = (float)img[((size_t)y0 * w + x1) * 3 + c];
-        const float p10 = (float)img[((size_t)y1 * w + x0) * 3 + c];
-        const float p11 = (float)img[((size_t)y1 * w + x1) * 3 + c];
-        const float top = p00 + (p01 - p00) * wx;
-        const float bot = p10 + (p11 - p10) * wx;
-        float v = (top + (bot - top) * wy) / 255.0f;
-        v = (v - mean[c]) / sd[c];
-        out[((size_t)b * 3 + c) * S * S + (size_t)yy * S + xx] = v;
-    }
-}
-
 // ---- legacy preprocess resize: src/image_io.cpp:249-275 (taps: resize_legacy.cpp)
 // One thread per output pixel: for each vertical tap, the horizontal weighted
 // sum of the row's taps, then the weighted sum of those rows, in tap order with
@@ -861,14 +827,6 @@ __global__ void k_dwconv_ln(const float* __restrict__ x, int B, int H, int W, in
 }
 
 }  // namespace
-
-cudaError_t preprocess_u8(const uint8_t* rgb, int B, int w, int h, int S, const float* mean3, const float* std3,
-                          float* out, cudaStream_t st) {
-    const size_t n = (size_t)B * S * S;
-    k_preprocess<<<cdiv(n, 256), 256, 0, st>>>(rgb, B, w, h, S, mean3[0], mean3[1], mean3[2], std3[0], std3[1],
-                                               std3[2], out);
-    return cudaGetLastError();
-}
 
 cudaError_t patch_im2col(const float* img, int B, int S, int p, int nw, int Kpad, __half* A, cudaStream_t st) {
     const int G = S / p, Tp = (G / nw) * (G / nw);

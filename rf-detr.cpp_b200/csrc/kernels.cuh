@@ -22,11 +22,6 @@ cudaError_t attention(const __half* q, const __half* k, const __half* v, int ldq
 cudaError_t attention_tc(const __half* q, const __half* k, const __half* v, int ldq, int ldk, int ldv, __half* o,
                          int ldo, int seq_len, int groups, int heads, float scale, int* err, cudaStream_t st);
 
-// uint8 HWC images [B][h][w][3] -> planar normalized f32 [B][3][S][S]
-// (bilinear, half-pixel centres, double-precision source coordinates).
-cudaError_t preprocess_u8(const uint8_t* rgb, int B, int w, int h, int S, const float* mean3, const float* std3,
-                          float* out, cudaStream_t st);
-
 // Patch im2col in windowed order: planar [B][3][S][S] -> A [B*NW*Tp][Kpad] f16,
 // K ordered (channel, ky, kx), zero padded to Kpad.
 cudaError_t patch_im2col(const float* img, int B, int S, int p, int nw, int Kpad, __half* A, cudaStream_t st);
