@@ -127,6 +127,9 @@ typedef struct {
     int      has_segmentation_head;
     size_t   n_tensors;
     char     variant[32];
+    int32_t  legacy_resize;  /* 1: images not at the model size take the legacy stb resize
+                                (rfdetr.preprocess.resize_mode legacy_stb, or absent as in files
+                                converted before the key existed); 0: the 1.9 bilinear path */
 } rfdetr_b200_model_info;
 rfdetr_status rfdetr_b200_inspect(const char* model_path, rfdetr_b200_model_info* out);
 

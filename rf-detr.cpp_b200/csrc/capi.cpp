@@ -690,6 +690,7 @@ extern "C" rfdetr_status rfdetr_b200_inspect(const char* path, rfdetr_b200_model
     out->has_segmentation_head = c.has_seg ? 1 : 0;
     out->n_tensors = m->file.tensors.size();
     std::strncpy(out->variant, c.variant.c_str(), sizeof(out->variant) - 1);
+    out->legacy_resize = c.bilinear_no_antialias ? 0 : 1;
     return st;
 }
 

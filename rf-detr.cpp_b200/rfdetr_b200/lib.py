@@ -52,7 +52,7 @@ class ModelInfo(C.Structure):
     _fields_ = [("image_size", C.c_uint32), ("patch_size", C.c_uint32), ("num_queries", C.c_uint32),
                 ("num_classes", C.c_uint32), ("dim", C.c_uint32), ("depth", C.c_uint32),
                 ("num_windows", C.c_uint32), ("dec_layers", C.c_uint32), ("has_segmentation_head", C.c_int),
-                ("n_tensors", C.c_size_t), ("variant", C.c_char * 32)]
+                ("n_tensors", C.c_size_t), ("variant", C.c_char * 32), ("legacy_resize", C.c_int32)]
 
 
 # name -> (restype, argtypes); every symbol declared in include/*.h

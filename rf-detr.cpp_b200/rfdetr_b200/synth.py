@@ -503,7 +503,9 @@ def write_gguf(path: str, variant_name: str, cfg: dict, state: "OrderedDict[str,
     w.add_array("rfdetr.class_names", names)
     w.add_array("rfdetr.preprocess.mean", np.array([0.485, 0.456, 0.406], np.float32).tolist())
     w.add_array("rfdetr.preprocess.std", np.array([0.229, 0.224, 0.225], np.float32).tolist())
-    w.add_string("rfdetr.preprocess.resize_mode", cfg.get("resize_mode", "bilinear_no_antialias"))
+    mode = cfg.get("resize_mode", "bilinear_no_antialias")
+    if mode is not None:  # None: no key, as in files converted before it existed
+        w.add_string("rfdetr.preprocess.resize_mode", mode)
     bb = cfg["backbone"]
     for k in ("dim", "depth", "heads", "ffn_dim", "num_windows"):
         w.add_uint32(f"rfdetr.backbone.{k}", bb[k])

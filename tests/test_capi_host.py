@@ -146,6 +146,27 @@ def test_gguf_reader_checks_lengths_against_the_file(tmp_path):
     assert status(b) == -6
 
 
+def test_resize_mode_key(tmp_path):
+    """rfdetr.preprocess.resize_mode (tests/test_model_loader.cpp:41-46,133-163 of the reference):
+    an absent key means the legacy stb resize, as in every file converted before the key existed;
+    the two values a converter writes select their path; an unknown value is
+    RFDETR_ERR_MODEL_FORMAT with a logged message that names the key."""
+    cases = {None: 1, "legacy_stb": 1, "bilinear_no_antialias": 0}
+    for mode, legacy in cases.items():
+        p = _write(tmp_path, f"mode-{mode}.gguf", meta_override={"resize_mode": mode}, dtype="f16")
+        st, info = lib.inspect(p)
+        assert st == 0 and info.legacy_resize == legacy, (mode, st, info.legacy_resize)
+    msgs = []
+    cb = lib.LOG_CB(lambda level, msg, user: msgs.append(msg.decode()))
+    L = lib.lib()
+    L.rfdetr_set_log_callback(cb, None)
+    try:
+        st, _ = lib.inspect(_write(tmp_path, "mode-bogus.gguf", meta_override={"resize_mode": "bogus"}, dtype="f16"))
+    finally:
+        L.rfdetr_set_log_callback(lib.LOG_CB(), None)
+    assert st == -6 and any("resize_mode" in m for m in msgs), (st, msgs)
+
+
 def test_inspect_rejects_unsupported_config(tmp_path):
     cfg = synth.get_variant("tiny")
     cfg["backbone"]["heads"] = 8  # head_dim 48: not implemented by the kernels
