@@ -380,6 +380,7 @@ def test_b200_entry_points_reject_null_handles():
     assert L.rfdetr_b200_sync(None) == -1
     # operator argument checks come before any launch: cudaErrorInvalidValue (1)
     assert L.rfdetr_b200_op_topk(None, 1, 1600, 91, 300, None, None) == 1
+    assert L.rfdetr_b200_op_resize_legacy(None, 1, 200, 160, None, 128, 128, None) == 1
     assert L.rfdetr_b200_detect_batch(None, None, 0, None, None, None) == -1
 
 
