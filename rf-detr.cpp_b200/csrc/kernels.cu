@@ -419,7 +419,7 @@ __device__ __forceinline__ uint32_t float_order(float f) {
 // One 1024-thread CTA per image.  Key of token t: (~order(max_c cls[t][c]) << 32) | t, so that
 // ascending keys are descending maxima with ties to the lower token, as the output wants.
 //  1. class maxima (the work is issue-bound on the CTA's one SM, so instructions are what count):
-//     a warp takes 8 tokens per round, issues its 24 class loads before any reduction, and
+//     a warp takes 8 tokens per step, issues their 24 class loads before any reduction, and
 //     reduces the 8 per-lane maxima with a transposed butterfly (9 shuffles for the 8 tokens);
 //  2. K < N: radix select of the K-th smallest key over 8-bit digits (the 4 score bytes, then
 //     the 2 low index bytes; N <= 4096 keeps index bits 16-31 zero) with warp-aggregated
