@@ -411,10 +411,15 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
 // rfdetr.h
 // ============================================================================
 
-extern "C" rfdetr_context* rfdetr_init(const rfdetr_params* params, rfdetr_status* out_status) {
+static rfdetr_context* rfdetr_init_body(const rfdetr_params* params, rfdetr_status* out_status) {
     int device = 0;
     if (const char* d = std::getenv("RFDETR_DEVICE")) device = std::atoi(d);
     return init_impl(params, device, 1, out_status);
+}
+
+extern "C" rfdetr_context* rfdetr_init(const rfdetr_params* params, rfdetr_status* out_status) {
+    return rfdetr_c_boundary_ptr<rfdetr_context>([&] { return rfdetr_init_body(params, out_status); },
+                                                 out_status, RFDETR_ERR_MODEL_LOAD);
 }
 
 extern "C" void rfdetr_free(rfdetr_context* ctx) { delete ctx; }
@@ -427,8 +432,9 @@ extern "C" uint32_t rfdetr_context_num_queries(const rfdetr_context* c) { return
 extern "C" uint32_t rfdetr_context_num_classes(const rfdetr_context* c) { return (c && c->model) ? c->model->cfg.num_classes : 0; }
 extern "C" size_t rfdetr_context_n_tensors(const rfdetr_context* c) { return (c && c->model) ? c->n_tensors : 0; }
 
-extern "C" rfdetr_status rfdetr_detect(rfdetr_context* ctx, const rfdetr_image* img, const rfdetr_detect_params* params,
-                                       rfdetr_detection** out_detections, size_t* out_n) {
+static rfdetr_status rfdetr_detect_body(rfdetr_context* ctx, const rfdetr_image* img,
+                                        const rfdetr_detect_params* params, rfdetr_detection** out_detections,
+                                        size_t* out_n) {
     if (out_detections) *out_detections = nullptr;
     if (out_n) *out_n = 0;
     if (!ctx || !img || !params || !out_detections || !out_n) return RFDETR_ERR_INVALID_ARG;
@@ -445,26 +451,46 @@ extern "C" rfdetr_status rfdetr_detect(rfdetr_context* ctx, const rfdetr_image* 
     return RFDETR_OK;
 }
 
+extern "C" rfdetr_status rfdetr_detect(rfdetr_context* ctx, const rfdetr_image* img,
+                                       const rfdetr_detect_params* params, rfdetr_detection** out_detections,
+                                       size_t* out_n) {
+    return rfdetr_c_boundary([&] { return rfdetr_detect_body(ctx, img, params, out_detections, out_n); },
+                             RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_INFERENCE);
+}
+
 // ============================================================================
 // rfdetr_b200.h
 // ============================================================================
 
-extern "C" rfdetr_context* rfdetr_b200_init(const rfdetr_params* params, const rfdetr_b200_params* b,
-                                            rfdetr_status* out_status) {
+static rfdetr_context* rfdetr_b200_init_body(const rfdetr_params* params, const rfdetr_b200_params* b,
+                                             rfdetr_status* out_status) {
     return init_impl(params, b ? b->device : 0, b && b->max_batch > 0 ? b->max_batch : 1, out_status,
                      b ? b->weight_type : 0);
 }
 
-extern "C" rfdetr_status rfdetr_b200_forward_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width,
-                                                 int height, float* out_logits, float* out_boxes, float* out_masks) {
+extern "C" rfdetr_context* rfdetr_b200_init(const rfdetr_params* params, const rfdetr_b200_params* b,
+                                            rfdetr_status* out_status) {
+    return rfdetr_c_boundary_ptr<rfdetr_context>([&] { return rfdetr_b200_init_body(params, b, out_status); },
+                                                 out_status, RFDETR_ERR_MODEL_LOAD);
+}
+
+static rfdetr_status rfdetr_b200_forward_rgb_body(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width,
+                                                  int height, float* out_logits, float* out_boxes, float* out_masks) {
     if (!ctx || !ctx->engine || !rgb || batch <= 0 || width <= 0 || height <= 0) return RFDETR_ERR_INVALID_ARG;
     rfdetr_status s = forward_rgb_impl(ctx, rgb, batch, width, height);
     if (s != RFDETR_OK) return s;
     return fetch_outputs(ctx, batch, out_logits, out_boxes, out_masks);
 }
 
-extern "C" rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width,
-                                                int height, float* out_logits, float* out_boxes, float* out_masks) {
+extern "C" rfdetr_status rfdetr_b200_forward_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width,
+                                                 int height, float* out_logits, float* out_boxes, float* out_masks) {
+    return rfdetr_c_boundary(
+        [&] { return rfdetr_b200_forward_rgb_body(ctx, rgb, batch, width, height, out_logits, out_boxes, out_masks); },
+        RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_INFERENCE);
+}
+
+static rfdetr_status rfdetr_b200_submit_rgb_body(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width,
+                                                 int height, float* out_logits, float* out_boxes, float* out_masks) {
     if (!ctx || !ctx->engine || !rgb || batch <= 0 || width <= 0 || height <= 0) return RFDETR_ERR_INVALID_ARG;
     rfb::Engine& e = *ctx->engine;
     if (RFB_CUDA_FAIL(cudaSetDevice(e.device()))) return RFDETR_ERR_INFERENCE;
@@ -543,7 +569,14 @@ extern "C" rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8
     return RFDETR_OK;
 }
 
-extern "C" rfdetr_status rfdetr_b200_wait_oldest(rfdetr_context* ctx) {
+extern "C" rfdetr_status rfdetr_b200_submit_rgb(rfdetr_context* ctx, const uint8_t* rgb, int batch, int width,
+                                                int height, float* out_logits, float* out_boxes, float* out_masks) {
+    return rfdetr_c_boundary(
+        [&] { return rfdetr_b200_submit_rgb_body(ctx, rgb, batch, width, height, out_logits, out_boxes, out_masks); },
+        RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_INFERENCE);
+}
+
+static rfdetr_status rfdetr_b200_wait_oldest_body(rfdetr_context* ctx) {
     if (!ctx || !ctx->engine) return RFDETR_ERR_INVALID_ARG;
     if (ctx->inflight.empty()) return RFDETR_OK;
     if (RFB_CUDA_FAIL(cudaSetDevice(ctx->engine->device()))) return RFDETR_ERR_INFERENCE;
@@ -554,7 +587,12 @@ extern "C" rfdetr_status rfdetr_b200_wait_oldest(rfdetr_context* ctx) {
     return ok ? RFDETR_OK : RFDETR_ERR_INFERENCE;
 }
 
-extern "C" rfdetr_status rfdetr_b200_wait(rfdetr_context* ctx) {
+extern "C" rfdetr_status rfdetr_b200_wait_oldest(rfdetr_context* ctx) {
+    return rfdetr_c_boundary([&] { return rfdetr_b200_wait_oldest_body(ctx); },
+                             RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_INFERENCE);
+}
+
+static rfdetr_status rfdetr_b200_wait_body(rfdetr_context* ctx) {
     if (!ctx || !ctx->engine) return RFDETR_ERR_INVALID_ARG;
     while (!ctx->inflight.empty()) {  // finished by the synchronizations below
         ctx->spare_events.push_back(ctx->inflight.front());
@@ -569,8 +607,13 @@ extern "C" rfdetr_status rfdetr_b200_wait(rfdetr_context* ctx) {
     return ctx->engine->finish();
 }
 
-extern "C" rfdetr_status rfdetr_b200_forward_planar(rfdetr_context* ctx, const float* planar, int batch,
-                                                    float* out_logits, float* out_boxes, float* out_masks) {
+extern "C" rfdetr_status rfdetr_b200_wait(rfdetr_context* ctx) {
+    return rfdetr_c_boundary([&] { return rfdetr_b200_wait_body(ctx); },
+                             RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_INFERENCE);
+}
+
+static rfdetr_status rfdetr_b200_forward_planar_body(rfdetr_context* ctx, const float* planar, int batch,
+                                                     float* out_logits, float* out_boxes, float* out_masks) {
     if (!ctx || !ctx->engine || !planar || batch <= 0) return RFDETR_ERR_INVALID_ARG;
     rfb::Engine& e = *ctx->engine;
     rfdetr_status s = e.reserve(batch);
@@ -585,8 +628,15 @@ extern "C" rfdetr_status rfdetr_b200_forward_planar(rfdetr_context* ctx, const f
     return fetch_outputs(ctx, batch, out_logits, out_boxes, out_masks);
 }
 
-extern "C" rfdetr_status rfdetr_b200_enqueue_device(rfdetr_context* ctx, const uint8_t* d_rgb, int batch, int width,
-                                                    int height) {
+extern "C" rfdetr_status rfdetr_b200_forward_planar(rfdetr_context* ctx, const float* planar, int batch,
+                                                    float* out_logits, float* out_boxes, float* out_masks) {
+    return rfdetr_c_boundary(
+        [&] { return rfdetr_b200_forward_planar_body(ctx, planar, batch, out_logits, out_boxes, out_masks); },
+        RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_INFERENCE);
+}
+
+static rfdetr_status rfdetr_b200_enqueue_device_body(rfdetr_context* ctx, const uint8_t* d_rgb, int batch, int width,
+                                                     int height) {
     if (!ctx || !ctx->engine || !d_rgb || batch <= 0 || width <= 0 || height <= 0) return RFDETR_ERR_INVALID_ARG;
     rfb::Engine& e = *ctx->engine;
     rfdetr_status s = e.reserve(batch);
@@ -594,9 +644,20 @@ extern "C" rfdetr_status rfdetr_b200_enqueue_device(rfdetr_context* ctx, const u
     return e.enqueue(batch, d_rgb, width, height);
 }
 
-extern "C" rfdetr_status rfdetr_b200_sync(rfdetr_context* ctx) {
+extern "C" rfdetr_status rfdetr_b200_enqueue_device(rfdetr_context* ctx, const uint8_t* d_rgb, int batch, int width,
+                                                    int height) {
+    return rfdetr_c_boundary([&] { return rfdetr_b200_enqueue_device_body(ctx, d_rgb, batch, width, height); },
+                             RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_INFERENCE);
+}
+
+static rfdetr_status rfdetr_b200_sync_body(rfdetr_context* ctx) {
     if (!ctx || !ctx->engine) return RFDETR_ERR_INVALID_ARG;
     return ctx->engine->finish();
+}
+
+extern "C" rfdetr_status rfdetr_b200_sync(rfdetr_context* ctx) {
+    return rfdetr_c_boundary([&] { return rfdetr_b200_sync_body(ctx); },
+                             RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_INFERENCE);
 }
 
 extern "C" rfdetr_status rfdetr_b200_device_outputs(rfdetr_context* ctx, const float** l, const float** b,
@@ -608,9 +669,9 @@ extern "C" rfdetr_status rfdetr_b200_device_outputs(rfdetr_context* ctx, const f
     return RFDETR_OK;
 }
 
-extern "C" rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfdetr_image* const* imgs, size_t n,
-                                                  const rfdetr_detect_params* params, rfdetr_detection** out_dets,
-                                                  size_t* out_counts) {
+static rfdetr_status rfdetr_b200_detect_batch_body(rfdetr_context* ctx, const rfdetr_image* const* imgs, size_t n,
+                                                   const rfdetr_detect_params* params, rfdetr_detection** out_dets,
+                                                   size_t* out_counts) {
     if (!ctx || !ctx->engine || !imgs || !params || !out_dets || !out_counts) return RFDETR_ERR_INVALID_ARG;
     for (size_t i = 0; i < n; ++i) { out_dets[i] = nullptr; out_counts[i] = 0; }
     if (n == 0) return RFDETR_OK;
@@ -640,6 +701,14 @@ extern "C" rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfd
     return RFDETR_OK;
 }
 
+extern "C" rfdetr_status rfdetr_b200_detect_batch(rfdetr_context* ctx, const rfdetr_image* const* imgs, size_t n,
+                                                  const rfdetr_detect_params* params, rfdetr_detection** out_dets,
+                                                  size_t* out_counts) {
+    return rfdetr_c_boundary(
+        [&] { return rfdetr_b200_detect_batch_body(ctx, imgs, n, params, out_dets, out_counts); },
+        RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_INFERENCE);
+}
+
 extern "C" int rfdetr_b200_device(const rfdetr_context* c) { return (c && c->engine) ? c->engine->device() : -1; }
 extern "C" int rfdetr_b200_mask_side(const rfdetr_context* c) { return (c && c->engine) ? c->engine->mask_side() : 0; }
 extern "C" int rfdetr_b200_kernels_per_forward(const rfdetr_context* c) {
@@ -647,16 +716,20 @@ extern "C" int rfdetr_b200_kernels_per_forward(const rfdetr_context* c) {
 }
 extern "C" void* rfdetr_b200_stream(const rfdetr_context* c) { return (c && c->engine) ? (void*)c->engine->stream() : nullptr; }
 
-extern "C" long long rfdetr_b200_trace(rfdetr_context* ctx, const char* name, int batch, float* out, size_t cap) {
+static long long rfdetr_b200_trace_body(rfdetr_context* ctx, const char* name, int batch, float* out, size_t cap) {
     if (!ctx || !ctx->engine || !name || !out || batch <= 0 || batch > ctx->engine->max_batch()) return -1;
     return ctx->engine->trace(name, batch, out, cap);
+}
+
+extern "C" long long rfdetr_b200_trace(rfdetr_context* ctx, const char* name, int batch, float* out, size_t cap) {
+    return rfdetr_c_boundary([&] { return rfdetr_b200_trace_body(ctx, name, batch, out, cap); }, -1LL, -1LL);
 }
 
 extern "C" void rfdetr_b200_profile_enable(rfdetr_context* ctx, int on) {
     if (ctx && ctx->engine) ctx->engine->set_profiling(on != 0);
 }
 
-extern "C" int rfdetr_b200_profile_read(rfdetr_context* ctx, char* names, int name_len, float* ms, int cap) {
+static int rfdetr_b200_profile_read_body(rfdetr_context* ctx, char* names, int name_len, float* ms, int cap) {
     if (!ctx || !ctx->engine) return -1;
     const auto prof = ctx->engine->profile();
     for (int i = 0; i < (int)prof.size() && i < cap; ++i) {
@@ -669,7 +742,11 @@ extern "C" int rfdetr_b200_profile_read(rfdetr_context* ctx, char* names, int na
     return (int)prof.size();
 }
 
-extern "C" rfdetr_status rfdetr_b200_inspect(const char* path, rfdetr_b200_model_info* out) {
+extern "C" int rfdetr_b200_profile_read(rfdetr_context* ctx, char* names, int name_len, float* ms, int cap) {
+    return rfdetr_c_boundary([&] { return rfdetr_b200_profile_read_body(ctx, names, name_len, ms, cap); }, -1, -1);
+}
+
+static rfdetr_status rfdetr_b200_inspect_body(const char* path, rfdetr_b200_model_info* out) {
     if (!path || !out) return RFDETR_ERR_INVALID_ARG;
     rfdetr_status st;
     std::unique_ptr<rfb::Model> m(rfb::model_load(path, &st));
@@ -692,6 +769,11 @@ extern "C" rfdetr_status rfdetr_b200_inspect(const char* path, rfdetr_b200_model
     std::strncpy(out->variant, c.variant.c_str(), sizeof(out->variant) - 1);
     out->legacy_resize = c.bilinear_no_antialias ? 0 : 1;
     return st;
+}
+
+extern "C" rfdetr_status rfdetr_b200_inspect(const char* path, rfdetr_b200_model_info* out) {
+    return rfdetr_c_boundary([&] { return rfdetr_b200_inspect_body(path, out); },
+                             RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_MODEL_FORMAT);
 }
 
 extern "C" int rfdetr_b200_dequantize(uint32_t type, const void* src, long long n, float* dst) {
@@ -773,7 +855,7 @@ int detect_common(rfdetr_handle_t handle, rfdetr_image* img, float threshold, ui
 
 }  // namespace
 
-extern "C" int rfdetr_capi_load(const char* model_path, int n_threads, rfdetr_handle_t* out_handle) {
+static int rfdetr_capi_load_body(const char* model_path, int n_threads, rfdetr_handle_t* out_handle) {
     if (!model_path || !out_handle) return -1;
     *out_handle = 0;
     rfdetr_params p{};
@@ -792,6 +874,11 @@ extern "C" int rfdetr_capi_load(const char* model_path, int n_threads, rfdetr_ha
     return 0;
 }
 
+extern "C" int rfdetr_capi_load(const char* model_path, int n_threads, rfdetr_handle_t* out_handle) {
+    return rfdetr_c_boundary([&] { return rfdetr_capi_load_body(model_path, n_threads, out_handle); },
+                             (int)RFDETR_ERR_OUT_OF_MEMORY, (int)RFDETR_ERR_MODEL_LOAD);
+}
+
 extern "C" int rfdetr_capi_unload(rfdetr_handle_t handle) {
     if (handle == 0) return 0;
     auto* h = reinterpret_cast<CapiHandle*>(handle);
@@ -800,8 +887,8 @@ extern "C" int rfdetr_capi_unload(rfdetr_handle_t handle) {
     return 0;
 }
 
-extern "C" int rfdetr_capi_detect_path(rfdetr_handle_t handle, const char* path, float threshold, uint32_t top_k,
-                                       char** out_json) {
+static int rfdetr_capi_detect_path_body(rfdetr_handle_t handle, const char* path, float threshold, uint32_t top_k,
+                                        char** out_json) {
     if (!handle || !path || !out_json) return -1;
     *out_json = nullptr;
     auto* h = reinterpret_cast<CapiHandle*>(handle);
@@ -815,8 +902,14 @@ extern "C" int rfdetr_capi_detect_path(rfdetr_handle_t handle, const char* path,
     return rc;
 }
 
-extern "C" int rfdetr_capi_detect_buffer(rfdetr_handle_t handle, const uint8_t* bytes, size_t len, float threshold,
-                                         uint32_t top_k, char** out_json) {
+extern "C" int rfdetr_capi_detect_path(rfdetr_handle_t handle, const char* path, float threshold, uint32_t top_k,
+                                       char** out_json) {
+    return rfdetr_c_boundary([&] { return rfdetr_capi_detect_path_body(handle, path, threshold, top_k, out_json); },
+                             (int)RFDETR_ERR_OUT_OF_MEMORY, (int)RFDETR_ERR_INFERENCE);
+}
+
+static int rfdetr_capi_detect_buffer_body(rfdetr_handle_t handle, const uint8_t* bytes, size_t len, float threshold,
+                                          uint32_t top_k, char** out_json) {
     if (!handle || !bytes || len == 0 || !out_json) return -1;
     *out_json = nullptr;
     auto* h = reinterpret_cast<CapiHandle*>(handle);
@@ -828,6 +921,13 @@ extern "C" int rfdetr_capi_detect_buffer(rfdetr_handle_t handle, const uint8_t* 
     const int rc = detect_common(handle, img, threshold, top_k, out_json);
     rfdetr_image_free(img);
     return rc;
+}
+
+extern "C" int rfdetr_capi_detect_buffer(rfdetr_handle_t handle, const uint8_t* bytes, size_t len, float threshold,
+                                         uint32_t top_k, char** out_json) {
+    return rfdetr_c_boundary(
+        [&] { return rfdetr_capi_detect_buffer_body(handle, bytes, len, threshold, top_k, out_json); },
+        (int)RFDETR_ERR_OUT_OF_MEMORY, (int)RFDETR_ERR_INFERENCE);
 }
 
 extern "C" void rfdetr_capi_free_string(char* s) { std::free(s); }

@@ -14,6 +14,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <stdexcept>
 
 namespace {
 
@@ -274,7 +275,7 @@ extern "C" rfdetr_image* rfdetr_image_load_buffer(const uint8_t* bytes, size_t l
     return img;
 }
 
-extern "C" rfdetr_image* rfdetr_image_load_file(const char* path, rfdetr_status* st) {
+static rfdetr_image* rfdetr_image_load_file_body(const char* path, rfdetr_status* st) {
     auto set = [&](rfdetr_status s) { if (st) *st = s; };
     if (!path) { set(RFDETR_ERR_INVALID_ARG); return nullptr; }
     FILE* f = std::fopen(path, "rb");
@@ -292,6 +293,11 @@ extern "C" rfdetr_image* rfdetr_image_load_file(const char* path, rfdetr_status*
     return rfdetr_image_load_buffer(buf.data(), buf.size(), st);
 }
 
+extern "C" rfdetr_image* rfdetr_image_load_file(const char* path, rfdetr_status* st) {
+    return rfdetr_c_boundary_ptr<rfdetr_image>([&] { return rfdetr_image_load_file_body(path, st); },
+                                               st, RFDETR_ERR_IO);
+}
+
 extern "C" rfdetr_image* rfdetr_image_from_rgb_buffer(const uint8_t* rgb, int width, int height, rfdetr_status* st) {
     auto set = [&](rfdetr_status s) { if (st) *st = s; };
     if (!rgb || width <= 0 || height <= 0) { set(RFDETR_ERR_INVALID_ARG); return nullptr; }
@@ -302,6 +308,10 @@ extern "C" rfdetr_image* rfdetr_image_from_rgb_buffer(const uint8_t* rgb, int wi
     } catch (const std::bad_alloc&) {
         delete img;
         set(RFDETR_ERR_OUT_OF_MEMORY);
+        return nullptr;
+    } catch (const std::length_error&) {  // more bytes than a buffer can hold: not a real image
+        delete img;
+        set(RFDETR_ERR_INVALID_ARG);
         return nullptr;
     }
     img->width = width;

@@ -112,7 +112,7 @@ int requantize_model(GgufFile* f, uint32_t type, int device, std::string* err) {
 
 }  // namespace rfb
 
-extern "C" rfdetr_status rfdetr_b200_quantize_gguf(const char* in_path, const char* out_path, int type, int device) {
+static rfdetr_status rfdetr_b200_quantize_gguf_body(const char* in_path, const char* out_path, int type, int device) {
     if (!in_path || !out_path) return RFDETR_ERR_INVALID_ARG;
     rfb::GgufFile f;
     std::string err;
@@ -132,4 +132,9 @@ extern "C" rfdetr_status rfdetr_b200_quantize_gguf(const char* in_path, const ch
         return (rfdetr_status)rc;
     }
     return RFDETR_OK;
+}
+
+extern "C" rfdetr_status rfdetr_b200_quantize_gguf(const char* in_path, const char* out_path, int type, int device) {
+    return rfdetr_c_boundary([&] { return rfdetr_b200_quantize_gguf_body(in_path, out_path, type, device); },
+                             RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_IO);
 }

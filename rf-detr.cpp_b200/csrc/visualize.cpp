@@ -5,6 +5,7 @@
 // when the box touches the image top).  Label glyphs are not rasterized.
 #include "rfdetr.h"
 
+#include "common.hpp"
 #include "image_io.hpp"
 
 #include <algorithm>
@@ -62,8 +63,8 @@ extern "C" void rfdetr_visualize_overlay_mask(rfdetr_image* img, rfdetr_detectio
     }
 }
 
-extern "C" rfdetr_status rfdetr_render(const rfdetr_image* img, const rfdetr_detection* dets, size_t n,
-                                       const char* out_path) {
+static rfdetr_status rfdetr_render_body(const rfdetr_image* img, const rfdetr_detection* dets, size_t n,
+                                        const char* out_path) {
     if (!img || !out_path || img->rgb.empty() || (n && !dets)) return RFDETR_ERR_INVALID_ARG;
     rfdetr_image copy = *img;
     for (size_t i = 0; i < n; ++i) rfdetr_visualize_overlay_mask(&copy, dets[i], 0.45f);
@@ -75,4 +76,10 @@ extern "C" rfdetr_status rfdetr_render(const rfdetr_image* img, const rfdetr_det
     const bool ok = std::fwrite(png.data(), 1, png.size(), f) == png.size();
     std::fclose(f);
     return ok ? RFDETR_OK : RFDETR_ERR_IO;
+}
+
+extern "C" rfdetr_status rfdetr_render(const rfdetr_image* img, const rfdetr_detection* dets, size_t n,
+                                       const char* out_path) {
+    return rfdetr_c_boundary([&] { return rfdetr_render_body(img, dets, n, out_path); },
+                             RFDETR_ERR_OUT_OF_MEMORY, RFDETR_ERR_IO);
 }

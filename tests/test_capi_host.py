@@ -319,6 +319,8 @@ def test_image_from_rgb_copies():
     assert data[5] == 5
     L.rfdetr_image_free(img)
     assert not L.rfdetr_image_from_rgb_buffer(None, 5, 4, C.byref(st)) and st.value == -1
+    # dimensions whose byte count no buffer can have are an invalid argument (nothing is read)
+    assert not L.rfdetr_image_from_rgb_buffer(rgb.ctypes.data, 2**31 - 1, 2**31 - 1, C.byref(st)) and st.value == -1
 
 
 def test_visualize_any_box(tmp_path):
