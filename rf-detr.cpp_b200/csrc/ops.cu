@@ -1,6 +1,8 @@
 // Operator entry points of rfdetr_b200.h: thin C wrappers over the kernels.
 #include "rfdetr_b200.h"
 
+#include "common.hpp"
+
 #include "gemm.cuh"
 #include "kernels.cuh"
 #include "mlp.cuh"
@@ -57,8 +59,8 @@ extern "C" int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes
                                               static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int rfdetr_b200_op_resize_legacy(const uint8_t* d_src, int batch, int w, int h, uint8_t* d_dst, int ow,
-                                           int oh, void* stream) {
+static int op_resize_legacy_body(const uint8_t* d_src, int batch, int w, int h, uint8_t* d_dst, int ow, int oh,
+                                 void* stream) {
     if (!d_src || !d_dst || batch < 0 || w <= 0 || h <= 0 || ow <= 0 || oh <= 0) return (int)cudaErrorInvalidValue;
     rfb::LegacyTapsDev t;
     cudaError_t e = rfb::upload_legacy_taps(w, h, ow, oh, &t);
@@ -68,6 +70,13 @@ extern "C" int rfdetr_b200_op_resize_legacy(const uint8_t* d_src, int batch, int
     const cudaError_t es = cudaStreamSynchronize(st);  // the taps are freed below
     cudaFree(t.base);
     return (int)(e != cudaSuccess ? e : es);
+}
+
+extern "C" int rfdetr_b200_op_resize_legacy(const uint8_t* d_src, int batch, int w, int h, uint8_t* d_dst, int ow,
+                                           int oh, void* stream) {
+    // the taps are built in host vectors: an allocation failure is reported, not thrown
+    return rfdetr_c_boundary([&] { return op_resize_legacy_body(d_src, batch, w, h, d_dst, ow, oh, stream); },
+                             (int)cudaErrorMemoryAllocation, (int)cudaErrorUnknown);
 }
 
 extern "C" int rfdetr_b200_op_topk(const float* d_cls, int batch, int n, int nc, int k, int32_t* d_idx,
