@@ -1,18 +1,21 @@
 #!/usr/bin/env python3
 """Throughput benchmark of the B200 RF-DETR engine.
 
-Workload (default): RF-DETR Base, Q8_0 weights, batch 32 per GPU, 560 x 560
-uniform-uint8 images (seeded), random-init weights written by the repository's
-GGUF writer (same bytes as the reference converter).  One step = one forward
-pass of the whole batch: GPU preprocess -> windowed DINOv2 backbone ->
-projector -> two-stage + top-K -> deformable decoder -> heads.
+Headline workload: RF-DETR Base, Q8_0 weights, batch 64 per GPU (the metric's
+batch), 560 x 560 uniform-uint8 images (seeded), random-init weights written by
+the repository's GGUF writer (same bytes as the reference converter).  One
+step = one forward pass of the whole batch: GPU preprocess -> windowed DINOv2
+backbone -> projector -> two-stage + top-K -> deformable decoder -> heads.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 runs one process per GPU (torchrun); each rank processes its own batch
 (weak scaling, no collective on the data path); timing is the max over ranks.
---global-batch B instead splits one batch of B images contiguously over the
-ranks (strong scaling).
+
+The same JSON line carries a `strong_scaling` object: RF-DETR Large, F16
+weights, 704 x 704, one global batch of 256 images split contiguously over the
+N ranks (256 / N per GPU), timed the same way (device-resident and end to
+end), with each rank's host -> device upload time of its share.
 
 Reported (one JSON line on rank 0):
   value       images/s, inputs already resident in HBM (device pointer API)
@@ -39,13 +42,19 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REPO, "rf-detr.cpp_b200"))
 
 METRIC = "images/sec per GPU and whole box (1/2/4/8 B200) at batch 64; p50 batch-1 ms"
-WORKLOAD = {"variant": "base", "dtype": "q8_0", "batch": 32, "image": 560}
+WORKLOAD = {"variant": "base", "dtype": "q8_0", "batch": 64, "image": 560}
+STRONG = {"variant": "large", "dtype": "f16", "global_batch": 256}
+L2_NOTE = "256 MB buffer written between timed steps (L2 is 126 MB)"
+# The reference's own published CPU latency for the headline model (ggml, batch 1, 8 threads).
+PUBLISHED_CPU = {"model": "base/q8_0", "median_ms": 145.7, "images_per_s": round(1000.0 / 145.7, 3),
+                 "cpu": "AMD Ryzen 9 9950X3D", "threads": 8,
+                 "source": "benchmarks/results/per_cell_latency.json"}
 
 
-def parse():
+def parse(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--variant", default=WORKLOAD["variant"])
@@ -53,8 +62,10 @@ def parse():
     p.add_argument("--batch", type=int, default=WORKLOAD["batch"])
     p.add_argument("--global-batch", type=int, default=0,
                    help="split this many images over the ranks (strong scaling) instead of --batch per rank")
+    p.add_argument("--strong-batch", type=int, default=STRONG["global_batch"],
+                   help="global batch of the strong-scaling leg (0 = skip the leg)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    return p.parse_args()
+    return p.parse_args(argv)
 
 
 def model_file(variant, dtype, pg):
@@ -65,8 +76,25 @@ def model_file(variant, dtype, pg):
     return replicas.create_once(path, lambda tmp: synth.write_model(tmp, variant, dtype, 0), pg)
 
 
+def headline_config(args, world):
+    """The `config` object of the line; the reference arm prints the same one."""
+    from rfdetr_b200 import synth
+    S = synth.get_variant(args.variant)["image_size"]
+    if args.global_batch > 0:
+        total = args.global_batch
+        per = f"global batch {total} split over {world} GPU(s)"
+    else:
+        total = args.batch * world
+        per = f"batch {args.batch} per GPU"
+    return {"workload": f"RF-DETR {args.variant} {args.dtype}, {per}, {S}x{S} uint8 images",
+            "global_batch": total, "per_gpu_batch": args.batch if args.global_batch <= 0 else None,
+            "image": S, "parallelism": f"dp{world} (independent replicas)", "l2": L2_NOTE}
+
+
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling around the timed region.  The sampler is started
+    before the warm-up and waited for (bounded) until its first sample, so a
+    short timed region on a busy host still gets samples."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -76,13 +104,19 @@ class Clocks:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.p = None
 
-    def start(self):
+    def start(self, wait_first_s=5.0):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
                                        "--format=csv,noheader,nounits", "-lms", "100"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
+            return
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < wait_first_s and self.p.poll() is None:
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if self.p:
@@ -128,9 +162,7 @@ def backbone_gemm_flops(cfg, batch):
     ntok = nw * nw * (ws * ws + 1)
     D, F = cfg["backbone"]["dim"], cfg["backbone"]["ffn_dim"]
     M = batch * ntok
-    per = {"qkv": 2 * M * D * 3 * D, "proj": 2 * M * D * D, "fc1": 2 * M * D * F, "fc2": 2 * M * F * D}
-    per["mlp"] = per["fc1"] + per["fc2"]  # the fused fc1 -> GELU -> fc2 launch
-    return per
+    return {"qkv": 2 * M * D * 3 * D, "proj": 2 * M * D * D, "fc1": 2 * M * D * F, "fc2": 2 * M * F * D}
 
 
 def peaks():
@@ -160,6 +192,17 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def cpu_oracle_run(path, n_images, seed, time_budget_s=None, threads=None):
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import numpy as np
@@ -181,8 +224,10 @@ def cpu_oracle_run(path, n_images, seed, time_budget_s=None, threads=None):
 
 def run_reference(args):
     """CPU arm: the reference cannot be built here (its ggml submodule is not
-    vendored), so its restated algorithm (the oracle) runs on the host cores."""
+    vendored), so its restated algorithm (the oracle) runs on the host cores,
+    one image of the headline batch per step (a bounded sample)."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return 0
     from rfdetr_b200 import replicas
@@ -191,21 +236,160 @@ def run_reference(args):
     cpu_oracle_run(path, max(args.warmup, 0), 7, threads=cores)
     n, dt = cpu_oracle_run(path, max(args.steps, 1), 11, threads=cores)
     v = n / dt
-    from rfdetr_b200 import synth
-    cfg = synth.get_variant(args.variant)
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "images/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "images/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / n * 1000, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded uint8 images, seeded random-init weights)",
-        "config": {"workload": f"RF-DETR {args.variant} {args.dtype}, {cfg['image_size']}x{cfg['image_size']}, "
-                               f"one image per step on the host CPU", "global_batch": 1},
+        "config": headline_config(args, world),
         "cpu_baseline": {"value": round(v, 4), "unit": "images/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} images, one per step, OpenMP over {cores} threads"},
+                         "cpu_model": cpu_model(), "nproc": os.cpu_count(),
+                         "sample": f"{n} images (one per step) of the workload's batch, restated reference "
+                                   f"forward (f32 activations x dequantized weights), OpenMP over {cores} threads"},
+        "published": PUBLISHED_CPU,
         "e2e": {"value": round(v, 4), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+class Leg:
+    """One engine context with its images: the device-resident and the end-to-end
+    timings of one workload on this rank."""
+
+    def __init__(self, path, local, lo, B, S):
+        import numpy as np
+        import torch
+        from rfdetr_b200 import lib
+        self.B, self.S, self.local = B, S, local
+        self.eng = lib.Engine(path, device=local, max_batch=B)
+        self.stream = torch.cuda.ExternalStream(self.eng.stream(), device=torch.device("cuda", local))
+        # image i of the (global) batch is drawn from seed 1000 + i, whatever rank owns it
+        self.imgs = np.stack([np.random.default_rng(1000 + lo + i).integers(0, 256, (S, S, 3), dtype=np.uint8)
+                              for i in range(B)])
+        self.d_imgs = torch.from_numpy(self.imgs).cuda(local)
+
+    def device(self, steps, warmup, flush, pg, clocks=None):
+        """Summed device ms of `steps` forwards from device-resident images, max over ranks."""
+        import torch
+        eng, B, S = self.eng, self.B, self.S
+        with torch.cuda.stream(self.stream):
+            if clocks:
+                clocks.start()
+            for _ in range(warmup):
+                eng.enqueue_device(self.d_imgs.data_ptr(), B, S, S)
+            eng.sync()
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            pg.barrier()
+            torch.cuda.synchronize()
+            for i in range(steps):
+                flush.zero_()  # L2 flush (256 MB > 126 MB L2), outside the timed interval
+                starts[i].record(self.stream)
+                eng.enqueue_device(self.d_imgs.data_ptr(), B, S, S)
+                ends[i].record(self.stream)
+            eng.sync()
+            torch.cuda.synchronize()
+            clk = clocks.stop() if clocks else None
+            pg.barrier()
+        ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+        return pg.max_over_ranks(ms), clk
+
+    def e2e(self, steps, warmup, pg):
+        """ms of `steps` pipelined submissions from pinned host images into pinned host
+        outputs (rfdetr_b200_submit_rgb / rfdetr_b200_wait), max over ranks; bytes per step."""
+        import torch
+        from rfdetr_b200 import lib
+        eng, B, S = self.eng, self.B, self.S
+        # every step uploads its images from host memory and downloads its logits and boxes into
+        # host memory; the upload of step i+1 and the download of step i-1 overlap the forward of
+        # step i.  The outputs are not read here, so two alternating host buffers suffice (a caller
+        # reading them gives each submission of a group its own buffers and reads after the wait).
+        h_imgs = torch.empty((B, S, S, 3), dtype=torch.uint8, pin_memory=True)
+        h_imgs.numpy()[:] = self.imgs
+        h_np = h_imgs.numpy()
+        nq, nc = eng.nq, eng.nc
+        h_lg = [torch.empty((B, nq, nc), dtype=torch.float32, pin_memory=True).numpy() for _ in range(2)]
+        h_bx = [torch.empty((B, nq, 4), dtype=torch.float32, pin_memory=True).numpy() for _ in range(2)]
+        L = lib.lib()
+
+        def call(i):
+            lib.check(L.rfdetr_b200_submit_rgb(eng.ctx, C.c_void_p(h_np.ctypes.data), B, S, S,
+                                               C.c_void_p(h_lg[i & 1].ctypes.data),
+                                               C.c_void_p(h_bx[i & 1].ctypes.data), None), "submit_rgb")
+
+        for i in range(warmup):
+            call(i)
+        lib.check(L.rfdetr_b200_wait(eng.ctx), "wait")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        pg.barrier()
+        torch.cuda.synchronize()
+        e0.record(self.stream)
+        for i in range(steps):
+            call(i)
+        # the downloads run on the context's own transfer stream: the end event goes on the engine
+        # stream after rfdetr_b200_wait, so the last step's download is inside the timed region
+        lib.check(L.rfdetr_b200_wait(eng.ctx), "wait")
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        pg.barrier()
+        ms = pg.max_over_ranks(e0.elapsed_time(e1))
+        return ms, B * S * S * 3, B * nq * (nc + 4) * 4, h_imgs
+
+    def upload(self, h_imgs, steps, pg):
+        """Mean ms of one host -> device copy of this rank's images from pinned memory
+        (all ranks copying at the same time), gathered on rank 0."""
+        import torch
+        dst = torch.empty_like(self.d_imgs)
+        s = torch.cuda.Stream(device=self.local)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        pg.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(s):
+            dst.copy_(h_imgs, non_blocking=True)  # warm-up
+            ev[0].record(s)
+            for _ in range(steps):
+                dst.copy_(h_imgs, non_blocking=True)
+            ev[1].record(s)
+        torch.cuda.synchronize()
+        pg.barrier()
+        return pg.gather_to_rank0(ev[0].elapsed_time(ev[1]) / steps)
+
+    def close(self):
+        self.eng.close()
+
+
+def strong_leg(args, rank, world, local, pg, flush):
+    """RF-DETR Large F16, one global batch split contiguously over the ranks."""
+    from rfdetr_b200 import replicas, synth
+    total = args.strong_batch
+    lo, hi = replicas.shard(total, rank, world)
+    B = hi - lo
+    S = synth.get_variant(STRONG["variant"])["image_size"]
+    path = model_file(STRONG["variant"], STRONG["dtype"], pg)
+    leg = Leg(path, local, lo, max(B, 1), S)
+    warm = max(args.warmup, 3)
+    dev_ms, _ = leg.device(args.steps, warm, flush, pg)
+    e2e_ms, h2d, d2h, h_imgs = leg.e2e(args.steps, warm, pg)
+    up = leg.upload(h_imgs, args.steps, pg)
+    leg.close()
+    shares = pg.gather_to_rank0(float(B))
+    return {
+        "workload": f"RF-DETR {STRONG['variant']} {STRONG['dtype']}, global batch {total} of {S}x{S} uint8 images "
+                    f"split contiguously over {world} GPU(s)",
+        "global_batch": total, "per_gpu_batch": [int(x) for x in shares] if shares else None,
+        "steps": args.steps, "warmup": warm,
+        "value": round(total * args.steps / (dev_ms / 1000.0), 2), "unit": "images/s",
+        "ms_per_step": round(dev_ms / args.steps, 4),
+        "e2e": {"value": round(total * args.steps / (e2e_ms / 1000.0), 2), "unit": "images/s",
+                "ms_per_step": round(e2e_ms / args.steps, 4), "h2d_bytes_per_step_per_gpu": h2d,
+                "d2h_bytes_per_step_per_gpu": d2h},
+        "upload_ms_per_step": {"per_rank": [round(x, 4) for x in up] if up else None,
+                               "max": round(max(up), 4) if up else None,
+                               "what": "one pinned host -> device copy of the rank's images, all ranks at once"},
+        "timing": "device: CUDA events around each forward, summed, max over ranks; e2e: events around the "
+                  "pipelined submissions, max over ranks",
+    }
 
 
 def main():
@@ -221,7 +405,6 @@ def main():
     rank, world, local = info.rank, info.world, info.local_rank
     torch.cuda.set_device(local)
     pg = replicas.ProcessGroup(info, "nccl", timeout_s=300.0, device=torch.device("cuda", local))
-    barrier = pg.barrier
 
     cfg = synth.get_variant(args.variant)
     S = cfg["image_size"]
@@ -232,86 +415,27 @@ def main():
             raise SystemExit("--global-batch smaller than the number of ranks")
     else:
         lo, B, scaling, total = rank * args.batch, args.batch, "weak", args.batch * world
+    warm = max(args.warmup, 3)
     path = model_file(args.variant, args.dtype, pg)
-    eng = lib.Engine(path, device=local, max_batch=B)
-    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
-    # image i of the (global) batch is drawn from seed 1000 + i, whatever rank owns it
-    imgs = np.stack([np.random.default_rng(1000 + lo + i).integers(0, 256, (S, S, 3), dtype=np.uint8)
-                     for i in range(B)])
-    d_imgs = torch.from_numpy(imgs).cuda(local)
+    leg = Leg(path, local, lo, B, S)
+    eng = leg.eng
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local}")
     torch.cuda.synchronize()
 
     # ---- device-resident throughput --------------------------------------
-    with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
-            eng.enqueue_device(d_imgs.data_ptr(), B, S, S)
-        eng.sync()
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        clocks = Clocks(local)
-        barrier()
-        torch.cuda.synchronize()
-        clocks.start()
-        for i in range(args.steps):
-            flush.zero_()  # L2 flush (256 MB > 126 MB L2), outside the timed interval
-            starts[i].record(stream)
-            eng.enqueue_device(d_imgs.data_ptr(), B, S, S)
-            ends[i].record(stream)
-        eng.sync()
-        torch.cuda.synchronize()
-        clk = clocks.stop()
-        barrier()
-    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    ms_max = pg.max_over_ranks(ms)
+    ms_max, clk = leg.device(args.steps, warm, flush, pg, clocks=Clocks(local))
     value = total * args.steps / (ms_max / 1000.0)
     launches = eng.kernels_per_forward() * args.steps
 
     # ---- end to end through the C API (pinned host buffers) -------------
-    # rfdetr_b200_submit_rgb: every step uploads its images from host memory and
-    # downloads its logits and boxes into host memory; the upload of step i+1
-    # and the download of step i-1 overlap the forward of step i.  The outputs are not read here, so two
-    # alternating host buffers suffice (a caller reading them gives each
-    # submission of a group its own buffers and reads after rfdetr_b200_wait).
-    h_imgs = torch.empty((B, S, S, 3), dtype=torch.uint8, pin_memory=True)
-    h_imgs.numpy()[:] = imgs
-    h_np = h_imgs.numpy()
-    nq, nc = eng.nq, eng.nc
-    h_lg = [torch.empty((B, nq, nc), dtype=torch.float32, pin_memory=True).numpy() for _ in range(2)]
-    h_bx = [torch.empty((B, nq, 4), dtype=torch.float32, pin_memory=True).numpy() for _ in range(2)]
-    L = lib.lib()
-
-    def e2e_call(i):
-        lib.check(L.rfdetr_b200_submit_rgb(eng.ctx, C.c_void_p(h_np.ctypes.data), B, S, S,
-                                           C.c_void_p(h_lg[i & 1].ctypes.data), C.c_void_p(h_bx[i & 1].ctypes.data),
-                                           None),
-                  "submit_rgb")
-
-    for i in range(max(args.warmup, 3)):
-        e2e_call(i)
-    lib.check(L.rfdetr_b200_wait(eng.ctx), "wait")
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for i in range(args.steps):
-        e2e_call(i)
-    # the downloads run on the context's own transfer stream: the end event goes
-    # on the engine stream after rfdetr_b200_wait, so the last step's download
-    # is inside the timed region (with a few microseconds of host wake-up)
-    lib.check(L.rfdetr_b200_wait(eng.ctx), "wait")
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_value = total * args.steps / (pg.max_over_ranks(e0.elapsed_time(e1)) / 1000.0)
-    h2d = B * S * S * 3
-    d2h = B * nq * (nc + 4) * 4
+    e2e_ms, h2d, d2h, _ = leg.e2e(args.steps, warm, pg)
+    e2e_value = total * args.steps / (e2e_ms / 1000.0)
 
     # ---- per-launch profile of one forward -> backbone GEMM roofline -----
     eng.profile_enable(True)
-    with torch.cuda.stream(stream):
+    with torch.cuda.stream(leg.stream):
         flush.zero_()
-        eng.enqueue_device(d_imgs.data_ptr(), B, S, S)
+        eng.enqueue_device(leg.d_imgs.data_ptr(), B, S, S)
         eng.sync()
     prof = eng.profile_read()
     eng.profile_enable(False)
@@ -336,22 +460,28 @@ def main():
     # ---- p50 batch-1 latency through rfdetr_detect ----------------------
     p50 = None
     if rank == 0:
+        L = lib.lib()
         st = C.c_int(0)
-        one = np.ascontiguousarray(imgs[0])
+        one = np.ascontiguousarray(leg.imgs[0])
         img = L.rfdetr_image_from_rgb_buffer(C.c_void_p(one.ctypes.data), S, S, C.byref(st))
         dp = lib.DetectParams(0.5, 300, None, 0)
         outp = C.POINTER(lib.Detection)()
         n = C.c_size_t(0)
         lat = []
-        for i in range(max(args.warmup, 3) + args.steps):
+        for i in range(warm + args.steps):
             t0 = time.perf_counter()
             lib.check(L.rfdetr_detect(eng.ctx, img, C.byref(dp), C.byref(outp), C.byref(n)), "rfdetr_detect")
             t1 = time.perf_counter()
             L.rfdetr_detections_free(outp, n.value)
-            if i >= max(args.warmup, 3):
+            if i >= warm:
                 lat.append((t1 - t0) * 1000.0)
         L.rfdetr_image_free(img)
         p50 = statistics.median(lat)
+    pg.barrier()
+    leg.close()
+
+    # ---- strong scaling: Large F16, global batch split over the ranks ---
+    strong = strong_leg(args, rank, world, local, pg, flush) if args.strong_batch > 0 else None
 
     # ---- CPU baseline (rank 0, N = 1) ------------------------------------
     cpu = None
@@ -359,40 +489,44 @@ def main():
         cores = host_threads()
         n_img, dt = cpu_oracle_run(path, 8, 5, time_budget_s=20.0, threads=cores)
         cpu = {"value": round(n_img / dt, 4), "unit": "images/s", "cores": cores, "kind": "port",
-               "sample": f"{n_img} of the {B} images of one step, restated reference forward (f32), "
-                         f"OpenMP over {cores} threads"}
+               "cpu_model": cpu_model(), "nproc": os.cpu_count(),
+               "sample": f"{n_img} images of the workload, restated reference forward (f32), "
+                         f"OpenMP over {cores} threads",
+               "published": PUBLISHED_CPU}
 
     if rank == 0:
+        config = headline_config(args, world)
+        config["per_gpu_batch"] = B
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max / args.steps, 4),
+            "steps": args.steps, "warmup": warm, "ms_per_step": round(ms_max / args.steps, 4),
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded uint8 images, seeded random-init weights)",
-            "config": {"workload": f"RF-DETR {args.variant} {args.dtype}, batch {B} per GPU, {S}x{S} uint8 images",
-                       "global_batch": total, "per_gpu_batch": B, "image": S,
-                       "parallelism": f"dp{world} (independent replicas)",
-                       "l2": "256 MB buffer written between timed steps (L2 is 126 MB)"},
-            "e2e": {"value": round(e2e_value, 2), "unit": "images/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+            "config": config,
+            "e2e": {"value": round(e2e_value, 2), "unit": "images/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world},
             "p50_batch1_ms": round(p50, 3) if p50 is not None else None,
             "gpu_launches": launches,
-            "roofline": {"kernel": "backbone linears: k_gemm qkv / proj and k_mlp (fc1 -> GELU -> fc2) launches",
+            "roofline": {"kernel": "backbone linears: k_gemm qkv / proj / fc1 (+GELU) / fc2 launches",
                          "bound": "tensor",
                          "achieved": round(achieved, 1) if achieved else None,
                          "peak": tf_sus, "unit": "TFLOP/s",
                          "frac": round(achieved / tf_sus, 4) if achieved else None,
                          "peak_source": f"{src} bf16 sustained (kernel timed inside the forward)",
                          "traffic": tr.get("bytes_per_launch") if tr else None,
+                         "timing": "per-launch CUDA events of one forward launched kernel by kernel outside "
+                                   "the CUDA graph the timed steps replay (conservative)",
                          "gemm_ms": round(gemm_ms, 4), "forward_ms": round(total_ms, 4),
                          "gemm_share": round(gemm_ms / total_ms, 4) if total_ms else None},
             "top_launches_ms": [[k, round(v, 4)] for k, v in top],
             "clocks": clk,
         }
+        if strong:
+            line["strong_scaling"] = strong
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     pg.barrier()  # rank 0's latency / CPU legs are done before any rank tears down
-    eng.close()
     pg.close()
     return 0
 

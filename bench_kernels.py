@@ -1,10 +1,9 @@
 """Micro-benchmark of single engine operators at model shapes.
 
-    python -m rfdetr_b200.kernels_bench gemm --m 51712 --n 1536 --k 384 [--epi 0 --act 1]
-    python -m rfdetr_b200.kernels_bench attn --seq 1616 --groups 32 --heads 6 --hd 64
-    python -m rfdetr_b200.kernels_bench deform --batch 32 --grid 40 --nq 300 --heads 16 --points 2
-    python -m rfdetr_b200.kernels_bench mlp --m 51712 --n 384 --k 1536      (D = n, hidden F = k)
-    python -m rfdetr_b200.kernels_bench topk --batch 1 --grid 40 --nc 91 --nq 300
+    python bench_kernels.py gemm --m 51712 --n 1536 --k 384 [--epi 0 --act 1]
+    python bench_kernels.py attn --seq 1616 --groups 32 --heads 6 --hd 64
+    python bench_kernels.py deform --batch 32 --grid 40 --nq 300 --heads 16 --points 2
+    python bench_kernels.py topk --batch 1 --grid 40 --nc 91 --nq 300
 
 Times `--iters` launches with CUDA events on the current stream (after
 `--warmup` launches) and prints one JSON line: ms per launch and achieved
@@ -18,15 +17,18 @@ kernel in isolation.
 import argparse
 import json
 import math
+import os
+import sys
 
 import torch
 
-from . import lib
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "rf-detr.cpp_b200"))
+from rfdetr_b200 import lib  # noqa: E402
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "attn", "deform", "mlp", "topk"])
+    ap.add_argument("op", choices=["gemm", "attn", "deform", "topk"])
     ap.add_argument("--m", type=int, default=51712)
     ap.add_argument("--n", type=int, default=1536)
     ap.add_argument("--k", type=int, default=384)
@@ -64,21 +66,6 @@ def main():
             assert rc == 0, rc
         flops = 2.0 * a.m * a.n * a.k
         name = f"gemm M={a.m} N={a.n} K={a.k} epi={a.epi} act={a.act}"
-    elif a.op == "mlp":
-        D, Fh = a.n, a.k
-        h = torch.randn(a.m, D, device=dev, generator=g).half()
-        w1 = (torch.randn(Fh, D, device=dev, generator=g) * 0.05).half()
-        w2 = (torch.randn(D, Fh, device=dev, generator=g) * 0.05).half()
-        b1 = torch.zeros(Fh, device=dev)
-        b2 = torch.zeros(D, device=dev)
-        x = torch.zeros(a.m, D, device=dev)
-
-        def run():
-            rc = L.rfdetr_b200_op_mlp(h.data_ptr(), D, w1.data_ptr(), D, b1.data_ptr(), w2.data_ptr(), Fh,
-                                      b2.data_ptr(), None, x.data_ptr(), D, a.m, D, Fh, st)
-            assert rc == 0, rc
-        flops = 4.0 * a.m * D * Fh
-        name = f"mlp M={a.m} D={D} F={Fh}"
     elif a.op == "deform":
         H, P, Dm, NQ, G, B = a.heads, a.points, a.dm, a.nq, a.grid, a.batch
         ld = H * P * 3

@@ -193,7 +193,10 @@ int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes, int batch
  * Catmull-Rom for a growing axis, Mitchell for a shrinking one, a copy for an
  * axis that keeps its size, clamped edges.  Outputs equal the library's except
  * for a byte differing by one where a value lies within float rounding of a
- * half.  Synchronizes `stream` before returning.  Device pointers. */
+ * half.  Device pointers.  The call allocates and frees its taps, so it
+ * synchronizes `stream` before returning (the host waits for the stream's
+ * earlier work too); a stream being captured into a CUDA graph is refused
+ * with cudaErrorStreamCaptureUnsupported before anything is enqueued. */
 int rfdetr_b200_op_resize_legacy(const uint8_t* d_src, int batch, int w, int h, uint8_t* d_dst, int ow, int oh,
                                  void* stream);
 
@@ -217,17 +220,6 @@ size_t rfdetr_b200_mask_bits_words(int img_w, int img_h);
 int rfdetr_b200_op_mask_bits(const float* d_masks, int batch, int nq, int side, const rfdetr_b200_det* d_dets,
                              const int* d_counts, int max_dets, int img_w, int img_h, uint32_t* d_bits, void* stream);
 
-/* Fused transformer MLP, the residual update of a DINOv2 block
- * (src/dinov2.cpp:93-101 with the layer scale and residual of :483-486):
- *   x[m] += ls * (GELU(h[m] . W1^T + b1) . W2^T + b2)
- * h f16 [M][D] (pitch ldh), W1 f16 [F][D] (pitch ldw1), b1 f32 [F], W2 f16
- * [D][F] (pitch ldw2), b2 f32 [D], ls f32 [D] or NULL (= 1), x f32 [M][D]
- * (pitch ldx) updated in place.  GELU is the erf form; its output is rounded to
- * f16 as the operand of the second product; the F-wide hidden activations stay
- * on chip.  Requires D a multiple of 128 up to 384 and F a multiple of 128. */
-int rfdetr_b200_op_mlp(const void* h, int ldh, const void* w1, int ldw1, const float* b1, const void* w2, int ldw2,
-                       const float* b2, const float* ls, float* x, int ldx, int M, int D, int F, void* stream);
-
 /* Deformable sampling of one level (value f16 [B*G*G][Dm], so_aw f32
  * [B*NQ][ld] = offsets (heads*points*2) then attention logits
  * (heads*points), refpoints f32 [B*NQ][4]) -> out f16 [B*NQ][Dm]. */
@@ -244,7 +236,9 @@ int rfdetr_b200_op_deform(const void* value, const float* so_aw, int ld_soaw, co
  * LayerNorm fused into the tcgen05 GEMM epilogue and the workspace is not
  * used; otherwise as an im2col into `workspace` followed by that GEMM.  The
  * workspace must hold rfdetr_b200_op_conv3x3_workspace(batch, h, w, c) bytes
- * of device memory either way. */
+ * of device memory either way.  src (and, on the im2col path, the workspace)
+ * must be 16-byte aligned with c and lds multiples of 8 and lds >= c;
+ * otherwise cudaErrorInvalidValue is returned before any launch. */
 size_t rfdetr_b200_op_conv3x3_workspace(int batch, int h, int w, int c);
 int rfdetr_b200_op_conv3x3(const void* src, int lds, int batch, int h, int w, int c, const void* weight, int oc,
                            const float* ln_g, const float* ln_b, float eps, int act, float* out32, int ld32,
@@ -262,7 +256,9 @@ int rfdetr_b200_op_conv3x3(const void* src, int lds, int batch, int h, int w, in
  * up the array's device address (cudaGetSymbolAddress) — make that first call
  * before any stream capture.  All calls on a device share the array: calls
  * whose work overlaps on the GPU race; calls in one stream are safe.  The
- * caller still passes inputs and outputs; arguments as rfdetr_b200_op_conv3x3. */
+ * caller still passes inputs and outputs; arguments as rfdetr_b200_op_conv3x3
+ * (it always takes the im2col path: src 16-byte aligned, c and lds multiples
+ * of 8, lds >= c, else cudaErrorInvalidValue before any launch). */
 int rfdetr_b200_op_conv3x3_noalloc(const void* src, int lds, int batch, int h, int w, int c, const void* weight,
                                    int oc, const float* ln_g, const float* ln_b, float eps, int act, float* out32,
                                    int ld32, void* out16, int ld16, void* stream);

@@ -72,9 +72,9 @@ __device__ __forceinline__ float ex2(float x) {
 // 2^x on the FMA pipe, two values at a time, for the share of the softmax
 // exponentials that the MUFU (ex2) cannot take without becoming the bound:
 // n = rint(x) (the 1.5 * 2^23 shift), f = x - n in [-1/2, 1/2], 2^f from a
-// degree-4 near-minimax polynomial (relative error <= 2.7e-6 in float32;
-// generated by exp2_poly.py in this directory), then n added to the exponent
-// field.  x is clamped at -125 (2^-125 is 0 once P is rounded to f16).
+// degree-4 near-minimax polynomial (relative error <= 2.7e-6 in float32; a
+// relative-error-weighted least-squares fit on [-1/2, 1/2] refined by Lawson's
+// iteratively reweighted least squares), then n added to the exponent field.  x is clamped at -125 (2^-125 is 0 once P is rounded to f16).
 constexpr float kExpShift = 12582912.0f;  // 1.5 * 2^23
 __device__ __forceinline__ float2 exp2_fma2(float2 x) {
     x = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));

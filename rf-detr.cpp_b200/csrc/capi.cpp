@@ -16,6 +16,7 @@
 #include "select.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <deque>
 #include <cstdlib>
 #include <cstring>
@@ -264,6 +265,16 @@ rfdetr_status upload_images(rfdetr_context* ctx, const rfdetr_image* const* imgs
     return RFDETR_OK;
 }
 
+// Host-side fault injection for the error-path tests: RFDETR_FAULT_INJECT=postprocess_alloc:N
+// makes the N-th post-processing call of the process (counting from 1) throw std::bad_alloc once
+// its first detection array has been handed out, as an allocation failure there would.
+bool inject_postprocess_fault() {
+    static std::atomic<long> calls{0};
+    const char* env = std::getenv("RFDETR_FAULT_INJECT");
+    if (!env || std::strncmp(env, "postprocess_alloc:", 18) != 0) return false;
+    return calls.fetch_add(1) + 1 == std::atol(env + 18);
+}
+
 void attach_names(const rfdetr_context* ctx, rfdetr_detection* d, size_t n) {
     const auto& names = ctx->model->cfg.class_names;
     for (size_t i = 0; i < n; ++i)
@@ -357,19 +368,27 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
         }
         if (RFB_CUDA_FAIL(cudaStreamSynchronize(st))) return RFDETR_ERR_INFERENCE;
     }
-    // masks to expand: (destination, bits) pairs, filled while building the records
+    // masks to expand: (destination, bits) pairs, filled while building the records.  Every
+    // allocation that can throw happens before the first array is built, and each array is
+    // handed to out_dets as soon as it exists, so a failure leaves nothing unowned.
+    for (int b = 0; b < batch; ++b) {
+        out_dets[b] = nullptr;
+        out_counts[b] = 0;
+    }
     std::vector<std::pair<uint8_t*, const uint32_t*>> jobs;
+    if (seg) jobs.reserve(kept);
+    const bool fault = inject_postprocess_fault();
     size_t off = 0;
     for (int b = 0; b < batch; ++b) {
         const int n = ctx->h_counts[b];
-        out_dets[b] = nullptr;
-        out_counts[b] = 0;
         if (n <= 0) continue;
         auto* d = static_cast<rfdetr_detection*>(std::calloc((size_t)n, sizeof(rfdetr_detection)));
         if (!d) {
             release_results(out_dets, out_counts, (size_t)b);
             return RFDETR_ERR_OUT_OF_MEMORY;
         }
+        out_dets[b] = d;
+        out_counts[b] = (size_t)n;
         for (int i = 0; i < n; ++i) {
             const rfdetr_b200_det& r = ctx->h_dets[(size_t)b * nq + i];
             d[i].class_id = (uint32_t)r.class_id;
@@ -385,8 +404,7 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
         }
         off += (size_t)n * words;
         attach_names(ctx, d, (size_t)n);
-        out_dets[b] = d;
-        out_counts[b] = (size_t)n;
+        if (fault) throw std::bad_alloc();
     }
     // expand the masks, over the context's host threads when there is enough of it
     const size_t pixels = jobs.size() * (size_t)w * h;
@@ -394,14 +412,22 @@ rfdetr_status postprocess_device(rfdetr_context* ctx, int batch, int w, int h, c
     auto work = [&](int t) {
         for (size_t j = (size_t)t; j < jobs.size(); j += (size_t)nt) g_mask_expand.run(jobs[j].second, w, h, jobs[j].first);
     };
-    if (nt <= 1) {
-        work(0);
-    } else {
-        std::vector<std::thread> pool;
-        for (int t = 1; t < nt; ++t) pool.emplace_back(work, t);
-        work(0);
-        for (auto& th : pool) th.join();
+    // workers 1 .. started-1 run on their own threads; if a thread cannot be created, the
+    // shares of the workers that did not start run here (the started ones are still joined)
+    std::vector<std::thread> pool;
+    int started = 1;
+    try {
+        if (nt > 1) pool.reserve((size_t)nt - 1);
+        for (int t = 1; t < nt; ++t) {
+            pool.emplace_back(work, t);
+            ++started;
+        }
+    } catch (const std::exception&) {
+        rfdetr_logf(RFDETR_LOG_WARN, "mask expansion: %d of %d host threads started", started, nt);
     }
+    work(0);
+    for (int t = started; t < nt; ++t) work(t);
+    for (auto& th : pool) th.join();
     return RFDETR_OK;
 }
 
@@ -443,7 +469,14 @@ static rfdetr_status rfdetr_detect_body(rfdetr_context* ctx, const rfdetr_image*
     rfdetr_status s = e.reserve(1);
     if (s == RFDETR_OK) s = upload_images(ctx, &img, 1, img->rgb.size());
     if (s == RFDETR_OK) s = e.enqueue(1, e.d_rgb(), img->width, img->height);
-    if (s == RFDETR_OK) s = postprocess_device(ctx, 1, img->width, img->height, params, out_detections, out_n);
+    if (s == RFDETR_OK) {
+        try {
+            s = postprocess_device(ctx, 1, img->width, img->height, params, out_detections, out_n);
+        } catch (...) {
+            release_results(out_detections, out_n, 1);  // a failed call hands back no array
+            throw;
+        }
+    }
     if (s != RFDETR_OK) {
         rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_detect: inference failed");
         return s == RFDETR_ERR_OUT_OF_MEMORY ? s : RFDETR_ERR_INFERENCE;
@@ -565,7 +598,13 @@ static rfdetr_status rfdetr_b200_submit_rgb_body(rfdetr_context* ctx, const uint
         ctx->spare_events.push_back(done);
         return RFDETR_ERR_INFERENCE;
     }
-    ctx->inflight.push_back(done);
+    try {
+        ctx->inflight.push_back(done);
+    } catch (...) {
+        // not tracked: rfdetr_b200_wait still covers the submission (it synchronizes the streams)
+        cudaEventDestroy(done);
+        throw;
+    }
     return RFDETR_OK;
 }
 
@@ -581,10 +620,10 @@ static rfdetr_status rfdetr_b200_wait_oldest_body(rfdetr_context* ctx) {
     if (ctx->inflight.empty()) return RFDETR_OK;
     if (RFB_CUDA_FAIL(cudaSetDevice(ctx->engine->device()))) return RFDETR_ERR_INFERENCE;
     cudaEvent_t ev = ctx->inflight.front();
-    ctx->inflight.pop_front();
-    const bool ok = !RFB_CUDA_FAIL(cudaEventSynchronize(ev));
+    // moved to the spares before it leaves the in-flight list, so a failing push leaves it owned
     ctx->spare_events.push_back(ev);
-    return ok ? RFDETR_OK : RFDETR_ERR_INFERENCE;
+    ctx->inflight.pop_front();
+    return RFB_CUDA_FAIL(cudaEventSynchronize(ev)) ? RFDETR_ERR_INFERENCE : RFDETR_OK;
 }
 
 extern "C" rfdetr_status rfdetr_b200_wait_oldest(rfdetr_context* ctx) {
@@ -690,7 +729,14 @@ static rfdetr_status rfdetr_b200_detect_batch_body(rfdetr_context* ctx, const rf
         rfdetr_status s = e.reserve(batch);
         if (s == RFDETR_OK) s = upload_images(ctx, imgs + i, (size_t)batch, (size_t)w * h * 3);
         if (s == RFDETR_OK) s = e.enqueue(batch, e.d_rgb(), w, h);
-        if (s == RFDETR_OK) s = postprocess_device(ctx, batch, w, h, params, out_dets + i, out_counts + i);
+        if (s == RFDETR_OK) {
+            try {
+                s = postprocess_device(ctx, batch, w, h, params, out_dets + i, out_counts + i);
+            } catch (...) {
+                release_results(out_dets, out_counts, j);  // this run's arrays and those before it
+                throw;
+            }
+        }
         if (s != RFDETR_OK && s != RFDETR_ERR_OUT_OF_MEMORY) s = RFDETR_ERR_INFERENCE;
         if (s != RFDETR_OK) {
             release_results(out_dets, out_counts, i);

@@ -67,6 +67,10 @@ extern "C" int rfdetr_b200_op_conv3x3_noalloc(const void* src, int lds, int batc
                                               void* stream) {
     if (!src || !weight || batch <= 0 || h <= 0 || w <= 0 || c <= 0) return (int)cudaErrorInvalidValue;
     if ((oc != 128 && oc != 256) || (act != rfb::ACT_NONE && act != rfb::ACT_SILU)) return (int)cudaErrorInvalidValue;
+    // the im2col reads src 16 bytes at a time: a misaligned src, or a pixel pitch shorter than the
+    // channel count, is refused here, before any address lookup or launch
+    if (!rfb::im2col3x3_source_ok(static_cast<const __half*>(src), lds, batch, h, w, c))
+        return (int)cudaErrorInvalidValue;
     const size_t need = (size_t)batch * h * w * 9 * c;
     if (need > kMaxColElems) {
         rfdetr_logf(RFDETR_LOG_ERROR,

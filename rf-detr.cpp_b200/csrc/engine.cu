@@ -7,24 +7,12 @@
 #include "common.hpp"
 #include "gemm.cuh"
 #include "kernels.cuh"
-#include "mlp.cuh"
 #include "sm100.cuh"
 
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
 
-// Build with -DRFB_FUSED_MLP=1 to run each backbone MLP as the single fused
-// kernel of mlp.cu (hidden activations kept on chip) instead of the fc1 and
-// fc2 GEMMs.  Measured on B200 (RF-DETR Base, batch 32, M = 51712): 208 us
-// per block fused vs 84 + 79 us for the two GEMMs.  With one 128-row tile per
-// SM the fused kernel streams W1 and W2 (2.36 MB) per tile through a
-// 96 KB shared-memory ring, and that stream runs latency-bound at 4.5 TB/s of
-// L2 reads (tensor pipe 31 % busy); it needs two-SM (cta_group::2) tiles to
-// halve the weight bytes per MMA.
-#ifndef RFB_FUSED_MLP
-#define RFB_FUSED_MLP 0
-#endif
 
 namespace rfb {
 
@@ -411,8 +399,7 @@ rfdetr_status Engine::alloc_activations(int B) {
         {(void**)&h16_, Mb * D_ * 2},
         {(void**)&qkv_, Mb * 3 * D_ * 2},
         {(void**)&attn_, Mb * D_ * 2},
-        // the fused MLP keeps the hidden activations on chip
-        {(void**)&f1_, RFB_FUSED_MLP && mlp_supported(D_, F_) ? (size_t)0 : Mb * F_ * 2},
+        {(void**)&f1_, Mb * F_ * 2},
         {(void**)&taps_, Mp * L_ * D_ * 2},
         {(void**)&cat_, Mp * (2 + bnecks_.size()) * Cb_ * 2},
         {(void**)&tmp128_, Mp * Cb_ * 2},
@@ -619,10 +606,6 @@ rfdetr_status Engine::enqueue(int B, const uint8_t* src_rgb, int src_w, int src_
     return RFDETR_OK;
 }
 
-// Build with -DRFB_FUSE_LN=1 to fuse the backbone LayerNorms into the residual GEMMs.
-#ifndef RFB_FUSE_LN
-#define RFB_FUSE_LN 0
-#endif
 
 rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int src_h) {
     if (B <= 0 || B > max_batch_) return RFDETR_ERR_INVALID_ARG;
@@ -672,23 +655,10 @@ rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int 
     L.check(write_cls_rows(x_, clsrow_, B, NW_, T_, D, st), "cls_rows");
 
     // ---- backbone blocks (src/dinov2.cpp:432-538)
-    // With RFB_FUSE_LN=1 every LayerNorm after the first is fused into the
-    // GEMM that updates the residual stream just before it (proj -> norm2,
-    // fc2 -> the next block's norm1), which writes x in f32 and LayerNorm(x)
-    // in f16 from the same tile.  That tile is 384 columns wide, so it has a
-    // single TMEM accumulator and its epilogue does not overlap the next
-    // tile's mainloop; measured on B200 (RF-DETR Base, batch 32) the separate
-    // TMA reduce-add GEMM + LayerNorm kernel is faster (6.73 vs 7.28 ms per
-    // forward; proj + norm2 37.9 + 23.7 µs vs 83.5 µs fused), so it is the default.
     const float scale = 1.0f / std::sqrt((float)(D / H_));
-    const bool fuse_ln = RFB_FUSE_LN && (D == 128 || D == 256 || D == 384);
-    const bool use_mlp = RFB_FUSED_MLP && mlp_supported(D, F_);
-    if (!blocks_.empty())
-        L.check(layernorm(x_, Mb, D, blocks_[0].ln1.g, blocks_[0].ln1.b, 1e-6f, nullptr, h16_, st), "ln1");
     for (size_t i = 0; i < blocks_.size(); ++i) {
         const Block& bk = blocks_[i];
-        const Block* next = i + 1 < blocks_.size() ? &blocks_[i + 1] : nullptr;
-        if (i > 0 && !fuse_ln) L.check(layernorm(x_, Mb, D, bk.ln1.g, bk.ln1.b, 1e-6f, nullptr, h16_, st), "ln1");
+        L.check(layernorm(x_, Mb, D, bk.ln1.g, bk.ln1.b, 1e-6f, nullptr, h16_, st), "ln1");
         L.gemm("qkv", h16_, D, Mb, bk.qkv, EPI_F16, ACT_NONE, nullptr, 0, qkv_, 3 * D);
         if (bk.global)
             L.check(attention_tc(qkv_, qkv_ + D, qkv_ + 2 * D, 3 * D, 3 * D, 3 * D, attn_, D, Ntok_, B, H_, scale, d_err_,
@@ -698,31 +668,10 @@ rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int 
             L.check(attention_tc(qkv_, qkv_ + D, qkv_ + 2 * D, 3 * D, 3 * D, 3 * D, attn_, D, T_, B * NW_, H_, scale,
                                  d_err_, st),
                     "attn_window");
-        if (fuse_ln) {
-            L.gemm("proj", attn_, D, Mb, bk.proj, EPI_RESID_LN, ACT_NONE, x_, D, h16_, D, bk.ls1, &bk.ln2, 1e-6f, x_,
-                   D);
-        } else {
-            L.gemm("proj", attn_, D, Mb, bk.proj, EPI_RESID, ACT_NONE, x_, D, nullptr, 0, bk.ls1);
-            L.check(layernorm(x_, Mb, D, bk.ln2.g, bk.ln2.b, 1e-6f, nullptr, h16_, st), "ln2");
-        }
-        if (use_mlp) {
-            // fc1 -> GELU -> fc2 -> layer scale -> residual in one kernel (mlp.cu)
-            MlpArgs m;
-            m.h = h16_; m.ldh = D;
-            m.w1 = bk.fc1.w; m.ldw1 = bk.fc1.ldw; m.b1 = bk.fc1.b;
-            m.w2 = bk.fc2.w; m.ldw2 = bk.fc2.ldw; m.b2 = bk.fc2.b;
-            m.ls = bk.ls2; m.x = x_; m.ldx = D;
-            m.M = Mb; m.D = D; m.F = F_; m.err = d_err_;
-            L.check(mlp_fused(m, st), "mlp");
-            if (fuse_ln && next) L.check(layernorm(x_, Mb, D, next->ln1.g, next->ln1.b, 1e-6f, nullptr, h16_, st), "ln1");
-        } else {
-            L.gemm("fc1", h16_, D, Mb, bk.fc1, EPI_F16, ACT_GELU, nullptr, 0, f1_, F_);
-            if (fuse_ln && next)
-                L.gemm("fc2", f1_, F_, Mb, bk.fc2, EPI_RESID_LN, ACT_NONE, x_, D, h16_, D, bk.ls2, &next->ln1, 1e-6f,
-                       x_, D);
-            else
-                L.gemm("fc2", f1_, F_, Mb, bk.fc2, EPI_RESID, ACT_NONE, x_, D, nullptr, 0, bk.ls2);
-        }
+        L.gemm("proj", attn_, D, Mb, bk.proj, EPI_RESID, ACT_NONE, x_, D, nullptr, 0, bk.ls1);
+        L.check(layernorm(x_, Mb, D, bk.ln2.g, bk.ln2.b, 1e-6f, nullptr, h16_, st), "ln2");
+        L.gemm("fc1", h16_, D, Mb, bk.fc1, EPI_F16, ACT_GELU, nullptr, 0, f1_, F_);
+        L.gemm("fc2", f1_, F_, Mb, bk.fc2, EPI_RESID, ACT_NONE, x_, D, nullptr, 0, bk.ls2);
         if (bk.tap >= 0)
             L.check(backbone_tap(x_, B, G, nw_, D, bbnorm_.g, bbnorm_.b, taps_, L_ * D, bk.tap * D, st), "tap");
     }

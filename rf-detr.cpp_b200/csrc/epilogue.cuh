@@ -17,9 +17,10 @@ namespace {
 //   GELU(v) = max(v, 0) - a e^{-a^2/2} R(a),  a = min(|v|, 6),
 //   R(a) = 0.5 erfcx(a / sqrt 2)
 // (erfcx = the scaled complementary error function).  -R is a polynomial,
-// a near-minimax fit on [0, 6] weighted by a e^{-a^2/2} (Lawson's
-// iteratively reweighted least squares; generated by gelu_poly.py in this
-// directory).  Evaluated in float32 with exp2, the absolute error of GELU for
+// a near-minimax fit on [0, 6] weighted by a e^{-a^2/2}: weighted least
+// squares on 200001 points against scipy.special.erfcx, refined by Lawson's
+// iteratively reweighted least squares (C. L. Lawson, 1961), 60 iterations.
+// Evaluated in float32 with exp2, the absolute error of GELU for
 // every input is <= 1.1e-7 with degree 10, <= 7.9e-7 with degree 8 and
 // <= 2.9e-6 with degree 7 (f16 spacing is 9.8e-7 at 0.002 and 2.4e-4 at 0.5);
 // the clamp at 6 adds < 7e-9.  One exp2 and (degree + 1) FMAs per value, no

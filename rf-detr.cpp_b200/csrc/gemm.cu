@@ -353,35 +353,6 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     tmem_ld32(tbase + c0 + 32, raw2);
                     tmem_wait_ld();
                     const bool tma_out = p.tma_out;
-                    if (tma_out && p.out32 && p.ln_pre32) {
-                        // the updated residual stream x (before normalisation): two 32-column f32 boxes
-#pragma unroll
-                        for (int hh = 0; hh < 2; ++hh) {
-                            if (lane == 0) bulk_wait_read<0>();
-                            __syncwarp();
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                const int jj = 4 * j;
-                                if (hh == 0)
-                                    st_shared_v4(swz(wbuf, lane, j), raw[jj], raw[jj + 1], raw[jj + 2], raw[jj + 3]);
-                                else
-                                    st_shared_v4(swz(wbuf, lane, j), raw2[jj], raw2[jj + 1], raw2[jj + 2], raw2[jj + 3]);
-                            }
-                            fence_async_smem();
-                            __syncwarp();
-                            if (lane == 0) {
-                                tma_store_3d(&tmO32, wptr, c0 + 32 * hh, m0w, b);
-                                bulk_commit();
-                            }
-                        }
-                    } else if (!tma_out && p.out32 && p.ln_pre32 && row_ok) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
-                        store_row_f32(p.out32 + boff + (size_t)m * p.ld32 + c0, v, c0, p.N);
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw2[j]);
-                        store_row_f32(p.out32 + boff + (size_t)m * p.ld32 + c0 + 32, v, c0 + 32, p.N);
-                    }
                     // y = act((x - mean) * rstd * g + b), in place, 16 columns at a time
 #pragma unroll
                     for (int sc = 0; sc < 64; sc += 16) {
@@ -407,7 +378,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         }
                     }
                     if (tma_out) {
-                        if (p.out32 && !p.ln_pre32) {
+                        if (p.out32) {
 #pragma unroll
                             for (int hh = 0; hh < 2; ++hh) {
                                 if (lane == 0) bulk_wait_read<0>();
@@ -456,7 +427,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                         for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
                             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(hh ? raw2[j] : raw[j]);
-                            if (p.out32 && !p.ln_pre32)
+                            if (p.out32)
                                 store_row_f32(p.out32 + boff + (size_t)m * p.ld32 + c0 + 32 * hh, v, c0 + 32 * hh, p.N);
                             if (p.out16)
                                 store_row_f16(p.out16 + boff + (size_t)m * p.ld16 + c0 + 32 * hh, v, c0 + 32 * hh, p.N);
@@ -835,12 +806,6 @@ void gemm_set_num_sms(int n) { g_num_sms = n > 0 ? n : 148; }
 cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
     if (!load_encode()) return cudaErrorNotSupported;
     GemmArgs a = a_in;
-    if (a.epi == EPI_RESID_LN) {
-        // out32 = resid + colscale * (acc + bias) (may alias resid), out16 = LayerNorm(out32)
-        if (!a.out32 || !a.out16 || a.act != ACT_NONE) return cudaErrorInvalidValue;
-        a.epi = EPI_LN;
-        a.ln_pre32 = 1;
-    }
     if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.batches <= 0) return cudaErrorInvalidValue;
     // TMA: 16-byte aligned base and row pitch
     if ((a.lda % 8) || (a.ldb % 8) || (((uintptr_t)a.A) & 15) || (((uintptr_t)a.B) & 15)) return cudaErrorInvalidValue;
@@ -871,7 +836,7 @@ cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
                                                      : launch<128, EPI_F32, ACT_NONE, true>(s, stream);
                     if (e != cudaSuccess) return e;
                     return splitk_layernorm(a.split_ws, ks, (long long)a.M * a.N, a.M, a.N, a.bias, nullptr, nullptr,
-                                            0, a.ln_g, a.ln_b, a.ln_eps, a.act, 0, nullptr, 0, a.out16, a.ld16, stream);
+                                            0, a.ln_g, a.ln_b, a.ln_eps, a.act, nullptr, 0, a.out16, a.ld16, stream);
                 }
             }
         }
@@ -916,7 +881,7 @@ cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
                 GemmArgs s = a;
                 s.epi = EPI_F32; s.act = ACT_NONE;
                 s.bias = nullptr; s.colscale = nullptr; s.resid = nullptr;
-                s.ln_g = nullptr; s.ln_b = nullptr; s.ln_pre32 = 0;
+                s.ln_g = nullptr; s.ln_b = nullptr;
                 s.out32 = a.split_ws; s.ld32 = a.N; s.out16 = nullptr; s.ld16 = 0;
                 s.batches = ks; s.a_batch_rows = 0; s.b_batch_rows = 0;
                 s.out_batch_stride = (long long)a.M * a.N;
@@ -924,7 +889,7 @@ cudaError_t gemm(const GemmArgs& a_in, cudaStream_t stream) {
                 const cudaError_t e = dispatch_bn<EPI_F32, ACT_NONE>(s, sbn, stream);
                 if (e != cudaSuccess) return e;
                 return splitk_layernorm(a.split_ws, ks, (long long)a.M * a.N, a.M, a.N, a.bias, a.colscale, a.resid,
-                                        a.ldr, a.ln_g, a.ln_b, a.ln_eps, a.act, a.ln_pre32, a.out32, a.ld32, a.out16,
+                                        a.ldr, a.ln_g, a.ln_b, a.ln_eps, a.act, a.out32, a.ld32, a.out16,
                                         a.ld16, stream);
             }
         }

@@ -16,9 +16,6 @@ enum GemmEpi : int {
     EPI_PATCH = 3,  // patch embed: windowed row remap, + bias + windowed pos-embed -> out32
     EPI_LN = 4,     // full-row LayerNorm(colscale * (acc + bias) [+ resid]) * g + b, act -> out32 / out16
                     // (BN == N = 128, 256 or 384)
-    EPI_RESID_LN = 5,  // out32 = resid + colscale * (acc + bias) (may alias resid; the residual stream
-                       // update) and out16 = LayerNorm(out32) * g + b: a residual GEMM fused with the
-                       // LayerNorm that reads its result
 };
 
 enum GemmAct : int { ACT_NONE = 0, ACT_GELU = 1, ACT_RELU = 2, ACT_SILU = 3 };
@@ -61,7 +58,6 @@ struct GemmArgs {
     int patch_rows = 0;    // patch rows per image
     int patch_ntok = 0;    // tokens per image
     const float* posw = nullptr;  // [ntok][N] windowed pos-embed
-    int ln_pre32 = 0;      // EPI_LN: out32 receives the sum before normalisation (set for EPI_RESID_LN)
     // Implicit-GEMM 3x3 convolution (stride 1, zero padding 1): when conv_src is
     // set, A is not read from memory as a matrix; row (b, y, x), column
     // (tap, c) of A is conv_src[b][y + tap/3 - 1][x + tap%3 - 1][c] (zero

@@ -859,7 +859,7 @@ template <int NV>
 __global__ void __launch_bounds__(256) k_splitk_ln(const float* __restrict__ part, int S, long long sstride, int rows,
                                                   const float* __restrict__ bias, const float* __restrict__ colscale,
                                                   const float* resid, int ldr, const float* __restrict__ g,
-                                                  const float* __restrict__ bb, float eps, int silu, int pre32,
+                                                  const float* __restrict__ bb, float eps, int silu,
                                                   float* out32, int ld32, __half* __restrict__ out16, int ld16) {
     constexpr int D = 128 * NV;
     const int lane = threadIdx.x & 31;
@@ -918,7 +918,7 @@ __global__ void __launch_bounds__(256) k_splitk_ln(const float* __restrict__ par
                 y.z = __fdividef(y.z, 1.0f + __expf(-y.z));
                 y.w = __fdividef(y.w, 1.0f + __expf(-y.w));
             }
-            if (out32) *reinterpret_cast<float4*>(out32 + (size_t)row * ld32 + c0) = pre32 ? v[i] : y;
+            if (out32) *reinterpret_cast<float4*>(out32 + (size_t)row * ld32 + c0) = y;
             if (out16) {
                 __half2 h0 = __floats2half2_rn(y.x, y.y), h1 = __floats2half2_rn(y.z, y.w);
                 *reinterpret_cast<uint2*>(out16 + (size_t)row * ld16 + c0) =
@@ -930,20 +930,20 @@ __global__ void __launch_bounds__(256) k_splitk_ln(const float* __restrict__ par
 
 cudaError_t splitk_layernorm(const float* part, int S, long long sstride, int rows, int D, const float* bias,
                              const float* colscale, const float* resid, int ldr, const float* g, const float* b,
-                             float eps, int act, int pre32, float* out32, int ld32, __half* out16, int ld16,
+                             float eps, int act, float* out32, int ld32, __half* out16, int ld16,
                              cudaStream_t st) {
     if (S < 1 || rows <= 0 || (act != 0 && act != 3) || !g || !b) return cudaErrorInvalidValue;
     const unsigned blocks = cdiv(rows, 8) < 148u * 6u ? cdiv(rows, 8) : 148u * 6u;
     const int silu = act == 3;
     if (D == 384)
         k_splitk_ln<3><<<blocks, 256, 0, st>>>(part, S, sstride, rows, bias, colscale, resid, ldr, g, b, eps, silu,
-                                               pre32, out32, ld32, out16, ld16);
+                                               out32, ld32, out16, ld16);
     else if (D == 256)
         k_splitk_ln<2><<<blocks, 256, 0, st>>>(part, S, sstride, rows, bias, colscale, resid, ldr, g, b, eps, silu,
-                                               pre32, out32, ld32, out16, ld16);
+                                               out32, ld32, out16, ld16);
     else if (D == 128)
         k_splitk_ln<1><<<blocks, 256, 0, st>>>(part, S, sstride, rows, bias, colscale, resid, ldr, g, b, eps, silu,
-                                               pre32, out32, ld32, out16, ld16);
+                                               out32, ld32, out16, ld16);
     else
         return cudaErrorInvalidValue;
     return cudaGetLastError();
@@ -984,8 +984,14 @@ cudaError_t backbone_tap(const float* x, int B, int G, int nw, int D, const floa
     return cudaGetLastError();
 }
 
+bool im2col3x3_source_ok(const __half* src, int lds, int B, int H, int W, int C) {
+    return src && B > 0 && H > 0 && W > 0 && C > 0 && C % 8 == 0 && lds % 8 == 0 && lds >= C &&
+           !((uintptr_t)src & 15);
+}
+
 cudaError_t im2col3x3(const __half* src, int lds, int B, int H, int W, int C, __half* A, cudaStream_t st) {
-    if (C % 8 || lds % 8) return cudaErrorInvalidValue;
+    // 16-byte loads of 8 channels at (pixel * lds + 8 * chunk) and 16-byte stores into A
+    if (!im2col3x3_source_ok(src, lds, B, H, W, C) || !A || ((uintptr_t)A & 15)) return cudaErrorInvalidValue;
     const size_t n = (size_t)B * H * W * 9 * (C / 8);
     k_im2col3x3<<<cdiv(n, 256), 256, 0, st>>>(src, lds, B, H, W, C, A);
     return cudaGetLastError();

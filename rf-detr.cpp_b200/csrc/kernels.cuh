@@ -42,11 +42,11 @@ cudaError_t write_cls_rows(float* x, const float* clsrow, int B, int NW, int T, 
 // LN(x) * g + b over rows of D (f32 in); writes y32 and/or y16 (either may
 // be null; y32 may alias x).
 // Split-K epilogue of a LayerNorm GEMM: x = sum over s < S of part[s] (in order) + bias, times
-// colscale, plus resid; y = act(LayerNorm(x) * g + b); out32 = pre32 ? x : y, out16 = y.  Rows of
+// colscale, plus resid; y = act(LayerNorm(x) * g + b); out32 = y, out16 = y.  Rows of
 // D = 128 / 256 / 384 (act: ACT_NONE or ACT_SILU).  out32 may alias resid.
 cudaError_t splitk_layernorm(const float* part, int S, long long sstride, int rows, int D, const float* bias,
                              const float* colscale, const float* resid, int ldr, const float* g, const float* b,
-                             float eps, int act, int pre32, float* out32, int ld32, __half* out16, int ld16,
+                             float eps, int act, float* out32, int ld32, __half* out16, int ld16,
                              cudaStream_t st);
 
 cudaError_t layernorm(const float* x, int rows, int D, const float* g, const float* b, float eps, float* y32,
@@ -58,8 +58,12 @@ cudaError_t backbone_tap(const float* x, int B, int G, int nw, int D, const floa
                          int ld, int col0, cudaStream_t st);
 
 // 3x3 same-padding im2col, channels-last: src rows [B*H*W] with `C` channels at
-// src + c (row pitch lds) -> A [B*H*W][9*C], K ordered (ky, kx, c).
+// src + c (row pitch lds) -> A [B*H*W][9*C], K ordered (ky, kx, c).  Moves 8
+// channels per 16-byte access: src and A 16-byte aligned, C and lds multiples
+// of 8 and lds >= C, else cudaErrorInvalidValue before any launch.
 cudaError_t im2col3x3(const __half* src, int lds, int B, int H, int W, int C, __half* A, cudaStream_t st);
+// The source-side part of that check (what a caller can test before it has A).
+bool im2col3x3_source_ok(const __half* src, int lds, int B, int H, int W, int C);
 
 // Copy f32 rows to f16, zeroing rows whose proposal is masked (G >= 50 only).
 cudaError_t mask_memory(const float* mem, int B, int G, int C, __half* out, cudaStream_t st);

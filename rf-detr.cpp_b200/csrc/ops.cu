@@ -5,7 +5,6 @@
 
 #include "gemm.cuh"
 #include "kernels.cuh"
-#include "mlp.cuh"
 #include "quant.cuh"
 #include "select.cuh"
 
@@ -13,8 +12,7 @@ extern "C" int rfdetr_b200_op_gemm(const void* A, int lda, const void* B, int ld
                                    int act, const float* bias, const float* colscale, const float* ln_g,
                                    const float* ln_b, float ln_eps, const float* resid, int ldr, float* out32,
                                    int ld32, void* out16, int ld16, void* stream) {
-    if (epi != rfb::EPI_F16 && epi != rfb::EPI_F32 && epi != rfb::EPI_RESID && epi != rfb::EPI_LN &&
-        epi != rfb::EPI_RESID_LN)
+    if (epi != rfb::EPI_F16 && epi != rfb::EPI_F32 && epi != rfb::EPI_RESID && epi != rfb::EPI_LN)
         return (int)cudaErrorInvalidValue;
     if ((epi == rfb::EPI_F16 && !out16) || ((epi == rfb::EPI_F32 || epi == rfb::EPI_RESID) && !out32))
         return (int)cudaErrorInvalidValue;
@@ -62,10 +60,16 @@ extern "C" int rfdetr_b200_op_select(const float* d_logits, const float* d_boxes
 static int op_resize_legacy_body(const uint8_t* d_src, int batch, int w, int h, uint8_t* d_dst, int ow, int oh,
                                  void* stream) {
     if (!d_src || !d_dst || batch < 0 || w <= 0 || h <= 0 || ow <= 0 || oh <= 0) return (int)cudaErrorInvalidValue;
-    rfb::LegacyTapsDev t;
-    cudaError_t e = rfb::upload_legacy_taps(w, h, ow, oh, &t);
-    if (e != cudaSuccess) return (int)e;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the taps are allocated and freed by the call, which therefore synchronizes the stream: a
+    // stream being captured into a graph is refused before anything is enqueued
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(st, &cap);
+    if (e != cudaSuccess) return (int)e;
+    if (cap != cudaStreamCaptureStatusNone) return (int)cudaErrorStreamCaptureUnsupported;
+    rfb::LegacyTapsDev t;
+    e = rfb::upload_legacy_taps(w, h, ow, oh, &t);
+    if (e != cudaSuccess) return (int)e;
     e = rfb::resize_legacy_rgb(d_src, batch, w, h, t, ow, oh, d_dst, st);
     const cudaError_t es = cudaStreamSynchronize(st);  // the taps are freed below
     cudaFree(t.base);
@@ -95,19 +99,6 @@ extern "C" int rfdetr_b200_op_mask_bits(const float* d_masks, int batch, int nq,
                                       static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int rfdetr_b200_op_mlp(const void* h, int ldh, const void* w1, int ldw1, const float* b1, const void* w2,
-                                  int ldw2, const float* b2, const float* ls, float* x, int ldx, int M, int D, int F,
-                                  void* stream) {
-    if (!h || !w1 || !w2 || !b1 || !b2 || !x || M < 0 || !rfb::mlp_supported(D, F)) return (int)cudaErrorInvalidValue;
-    rfb::MlpArgs a;
-    a.h = static_cast<const __half*>(h); a.ldh = ldh;
-    a.w1 = static_cast<const __half*>(w1); a.ldw1 = ldw1; a.b1 = b1;
-    a.w2 = static_cast<const __half*>(w2); a.ldw2 = ldw2; a.b2 = b2;
-    a.ls = ls; a.x = x; a.ldx = ldx;
-    a.M = M; a.D = D; a.F = F;
-    return (int)rfb::mlp_fused(a, static_cast<cudaStream_t>(stream));
-}
-
 extern "C" int rfdetr_b200_op_deform(const void* value, const float* so_aw, int ld_soaw, const float* refp, int batch,
                                      int nq, int grid, int heads, int points, int dm, void* out, void* stream) {
     return (int)rfb::deform_sample(static_cast<const __half*>(value), so_aw, ld_soaw, refp, batch, nq, grid, heads,
@@ -125,6 +116,7 @@ extern "C" int rfdetr_b200_op_conv3x3(const void* src, int lds, int batch, int h
                                       void* stream) {
     const size_t need = rfdetr_b200_op_conv3x3_workspace(batch, h, w, c);
     if (!src || !weight || !workspace || need == 0 || workspace_bytes < need) return (int)cudaErrorInvalidValue;
+    if ((size_t)batch * h * w > (size_t)INT32_MAX) return (int)cudaErrorInvalidValue;
     if ((oc != 128 && oc != 256) || (act != rfb::ACT_NONE && act != rfb::ACT_SILU)) return (int)cudaErrorInvalidValue;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (c % 64 == 0 && w <= 128) {
@@ -141,6 +133,7 @@ extern "C" int rfdetr_b200_op_conv3x3(const void* src, int lds, int batch, int h
         return (int)rfb::gemm(a, st);
     }
     __half* col = static_cast<__half*>(workspace);
+    // im2col3x3 refuses a misaligned src / workspace or lds < c before launching
     cudaError_t e = rfb::im2col3x3(static_cast<const __half*>(src), lds, batch, h, w, c, col, st);
     if (e != cudaSuccess) return (int)e;
     rfb::GemmArgs a;

@@ -5,8 +5,9 @@ Runs the reference's own `write_gguf` + `build_tensor_name_map`
 dict and records the SHA-256 of each written file.  The repository's writer
 (rfdetr_b200.synth) must reproduce these bytes exactly.
 
-Needs a checkout of localai-org/rf-detr.cpp (default /root/reference); run
-from the repository root:  python tests/golden/gen_converter_golden.py
+Needs a checkout of localai-org/rf-detr.cpp named by RFDETR_REFERENCE; run
+from the repository root:
+    RFDETR_REFERENCE=<checkout> python tests/golden/gen_converter_golden.py
 """
 import hashlib
 import json
@@ -16,7 +17,10 @@ import tempfile
 
 REPO = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, os.path.join(REPO, "rf-detr.cpp_b200"))
-REF = os.environ.get("RFDETR_REFERENCE", "/root/reference")
+REF = os.environ.get("RFDETR_REFERENCE")
+if not REF or not os.path.isfile(os.path.join(REF, "scripts", "convert_rfdetr_to_gguf.py")):
+    raise SystemExit("set RFDETR_REFERENCE to a checkout of localai-org/rf-detr.cpp "
+                     "(scripts/convert_rfdetr_to_gguf.py is read from it)")
 sys.path.insert(0, os.path.join(REF, "scripts"))
 
 import torch  # noqa: E402

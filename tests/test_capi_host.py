@@ -400,3 +400,34 @@ def test_init_errors_without_touching_the_gpu(tmp_path):
     assert not L.rfdetr_init(C.byref(p), C.byref(st)) and st.value == -7
     assert any("missing tensor" in m for m in msgs)
     L.rfdetr_set_log_callback(lib.LOG_CB(), None)
+
+
+@pytest.mark.parametrize("noalloc", [False, True])
+def test_conv3x3_rejects_misaligned_source_before_any_launch(noalloc):
+    """The im2col path of both ConvX entry points reads `src` 8 channels (16 bytes) at a
+    time: a source that is not 16-byte aligned, a pixel pitch shorter than the channel
+    count, or a channel count that is not a multiple of 8 is refused with
+    cudaErrorInvalidValue (1) before any device work.  The pointers are fake addresses that
+    nothing may touch (c = 96 selects the im2col path of the workspace variant)."""
+    L = lib.lib()
+    src, w, g, out = C.c_void_p(0x100000), C.c_void_p(0x200000), C.c_void_p(0x300000), C.c_void_p(0x400000)
+    ws = C.c_void_p(0x500000)
+    B, H, W, Cin = 1, 8, 8, 96
+    ws_bytes = L.rfdetr_b200_op_conv3x3_workspace(B, H, W, Cin)
+
+    def call(s, lds, c):
+        if noalloc:
+            return L.rfdetr_b200_op_conv3x3_noalloc(s, lds, B, H, W, c, w, 128, g, g, 1e-6, 0, out, 128, None, 0,
+                                                    None)
+        return L.rfdetr_b200_op_conv3x3(s, lds, B, H, W, c, w, 128, g, g, 1e-6, 0, out, 128, None, 0, ws,
+                                        ws_bytes, None)
+
+    assert call(C.c_void_p(0x100002), Cin, Cin) == 1   # src one f16 element past a 16-byte boundary
+    assert call(src, Cin - 8, Cin) == 1                  # lds < c
+    assert call(src, Cin + 4, Cin) == 1                  # lds not a multiple of 8
+    assert call(src, 100, 100) == 1                      # c not a multiple of 8
+    if not noalloc:
+        # a misaligned workspace is refused as well
+        assert L.rfdetr_b200_op_conv3x3(src, Cin, B, H, W, Cin, w, 128, g, g, 1e-6, 0, out, 128, None, 0,
+                                        C.c_void_p(0x500008), ws_bytes, None) == 1
+

@@ -1,18 +1,34 @@
 """End-to-end parity on the B200: the CUDA engine (through the C ABI) against
 the CPU oracle on the same seeded synthetic models and images.
 
-Metric: rel = max|gpu - oracle| / max|oracle| per tensor.  Tolerances on the
-outputs (class logits, boxes): 1e-3 for F32/F16 weights, 2e-2 for Q8_0/Q4_K.
-The engine computes GEMM operands in f16 with f32 accumulation and an f32
-residual stream; the oracle is f32 throughout.  Intermediate stages
-(projector output, two-stage class logits) are checked at 3x the output
-tolerance: they are diagnostics that localize a regression, the contract is
-on the outputs.
+Metrics, per output tensor (class logits, boxes):
+  rel       max|gpu - oracle| / max|oracle|                                   <= tol
+  el_p50    median over elements of |gpu - oracle| / max(|oracle|, tol * max|oracle|)  <= tol
+  el_p90, el_max   the same ratio's 90th percentile and maximum (reported)
+with tol = 1e-3 for F32/F16 weights and 2e-2 for Q8_0/Q4_K.  The element-wise
+figures measure each value against its own magnitude; the floor (tol x the
+tensor's largest magnitude) keeps a value that is zero in the oracle from
+dividing by zero.  Their tail is not held to tol: rounding the activations to
+f16 gives errors of absolute, not relative, size, so logits near zero carry a
+large relative error, and the reference's own arithmetic does the same (the
+oracle's mode ii against its mode i on Nano F16: p50 2.3e-4, p90 1.4e-3, max
+0.16; on a Q8_0 model: p50 5.9e-3, p90 3.4e-2).  The engine computes GEMM operands in f16 with
+f32 accumulation and an f32 residual stream; the oracle is f32 throughout
+(mode i).  For Q8_0 / Q4_K models the oracle is also run in mode ii, which
+rounds activations before each weight product the way ggml's CPU vec-dot does
+(F16 / Q8_0 / Q8_K blocks), and the distances to both are printed and checked.
 
-Top-K: positions may differ only between near-tied tokens (oracle scores
-within the tolerance); the decoder and heads are then compared with the
-oracle forced onto the engine's selection, so both see identical queries.
+Top-K: the selected token must be the oracle's at every rank, except where
+the two tokens' oracle class scores differ by at most tol x the largest
+score (a near-tie the tolerance cannot order).  The decoder and heads are then
+compared with the oracle forced onto the engine's selection, so both see the
+same queries.  Masks: mean IoU of the thresholded masks (logit > 0, i.e.
+sigmoid > 0.5) per query >= 0.99, queries empty in both counting as 1.
+Intermediate stages (projector output, two-stage class logits) are checked at
+3x the output tolerance as diagnostics that localize a regression.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -27,29 +43,73 @@ def rel(a, b):
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
 
+def rel_elementwise(a, b, tol):
+    """(median, 90th percentile, max) over elements of |a - b| / max(|b|, tol * max|b|)."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    den = np.maximum(np.abs(b), tol * max(np.abs(b).max(), 1e-30))
+    r = np.abs(a - b) / den
+    p50, p90 = np.percentile(r, [50, 90])
+    return float(p50), float(p90), float(r.max())
+
+
+def mask_iou(gpu, ref):
+    """(mean, min) over queries of the IoU of the masks thresholded at logit > 0."""
+    g = np.asarray(gpu).reshape(gpu.shape[0], -1) > 0
+    r = np.asarray(ref).reshape(ref.shape[0], -1) > 0
+    inter = (g & r).sum(1)
+    union = (g | r).sum(1)
+    iou = np.where(union > 0, inter / np.maximum(union, 1), 1.0)
+    return float(iou.mean()), float(iou.min())
+
+
 def _images(S, n, seed):
     rng = np.random.default_rng(seed)
     return rng.integers(0, 256, (n, S, S, 3), dtype=np.uint8)
 
 
 def check_topk(gpu_idx, ora_idx, scores, tol):
-    """Same token at each rank, except swaps among near-tied scores.
+    """Same token at each rank as the oracle's own selection, except where the two
+    tokens' oracle scores differ by at most tol x max|score| (a near-tie).
 
-    The selection key is a class score, an intermediate value that is itself
-    allowed 3 x `tol` relative error, so two tokens whose oracle scores differ
-    by less than that may legitimately trade places.  The reference's own
-    arithmetic does the same: rounding activations to f16 before each F16
-    matmul, as ggml's CPU path does, already swaps 44 (Nano F16), 64 (Large
-    F16) and 248 (Base Q8_0) of the top-K ranks against exact f32.
-    """
+    Returns (swaps, largest gap / max|score|)."""
     gpu_idx = np.asarray(gpu_idx, np.int64)
     ora_idx = np.asarray(ora_idx, np.int64)
     smax = np.abs(scores).max()
     diff = gpu_idx != ora_idx
+    gap = 0.0
     if diff.any():
-        gap = np.abs(scores[gpu_idx[diff]] - scores[ora_idx[diff]]).max()
-        assert gap <= 3 * tol * smax, f"top-K differs beyond near-ties: gap {gap}"
-    return int(diff.sum())
+        gap = float(np.abs(scores[gpu_idx[diff]] - scores[ora_idx[diff]]).max() / smax)
+        assert gap <= tol, f"top-K differs beyond near-ties: gap {gap:.3g} x max score > {tol}"
+    return int(diff.sum()), gap
+
+
+def compare_image(ora, x, lg, bx, mk, topk, cls_gpu, cls_o, own_topk, tol, mode2=False):
+    """Every parity figure of one image; asserts the contract and returns the report."""
+    r = {}
+    r["topk_swaps"], r["topk_gap"] = check_topk(topk, own_topk, cls_o.max(1), tol)
+    r["cls_all"] = rel(cls_gpu, cls_o)
+    forced = ora.forward(x, force_topk=topk)
+    for name, got, want in (("logits", lg, forced["logits"]), ("boxes", bx, forced["boxes"])):
+        r[name] = rel(got, want)
+        r[name + "_el_p50"], r[name + "_el_p90"], r[name + "_el_max"] = rel_elementwise(got, want, tol)
+    if mk is not None:
+        r["masks"] = rel(mk, forced["masks"])
+        r["mask_iou_mean"], r["mask_iou_min"] = mask_iou(mk, forced["masks"])
+    if mode2:
+        # oracle mode ii (ggml-like activation rounding) on the same queries
+        f2 = ora.forward(x, act_round=1, force_topk=topk)
+        r["logits_mode2"] = rel(lg, f2["logits"])
+        r["boxes_mode2"] = rel(bx, f2["boxes"])
+        r["mode2_vs_mode1_logits"] = rel(f2["logits"], forced["logits"])
+    assert r["cls_all"] < 3 * tol, r
+    for name in ("logits", "boxes"):
+        assert r[name] < tol and r[name + "_el_p50"] < tol, (name, r)
+        if mode2:
+            assert r[name + "_mode2"] < tol, (name, r)
+    if mk is not None:
+        assert r["mask_iou_mean"] >= 0.99, r
+    return r
 
 
 CASES = [("tiny", "f32", 2), ("tiny", "f16", 1), ("tiny", "q8_0", 1), ("tiny", "q4_K", 1),
@@ -72,6 +132,7 @@ def test_engine_matches_oracle(variant, dtype, batch, make_model):
     cls_gpu = eng.trace("two_stage.cls_all", batch).reshape(batch, G * G, NC)
     topk_gpu = eng.trace("topk", batch).reshape(batch, NQ).astype(np.int64)
     proj_gpu = eng.trace("projector.output", batch).reshape(batch, G * G, -1)
+    eng.close()
     tol = TOL[dtype]
     report = []
     for b in range(batch):
@@ -79,22 +140,12 @@ def test_engine_matches_oracle(variant, dtype, batch, make_model):
         own = ora.forward(x, trace=True)
         tr = own["trace"]
         cls_o = tr["two_stage.cls_all"].reshape(G * G, NC)
-        forced = ora.forward(x, force_topk=topk_gpu[b])
-        r = {"projector": rel(proj_gpu[b], tr["projector.output"].reshape(G * G, -1)),
-             "cls_all": rel(cls_gpu[b], cls_o),
-             "topk_swaps": check_topk(topk_gpu[b], own["topk"], cls_o.max(1), tol),
-             "logits": rel(lg[b], forced["logits"]), "boxes": rel(bx[b], forced["boxes"])}
-        if mk is not None:
-            r["masks"] = rel(mk[b], forced["masks"])
-            r["mask_sign_agree"] = float(((mk[b] > 0) == (forced["masks"] > 0)).mean())
+        r = compare_image(ora, x, lg[b], bx[b], None if mk is None else mk[b], topk_gpu[b], cls_gpu[b], cls_o,
+                          own["topk"], tol, mode2=dtype in ("q8_0", "q4_K"))
+        r["projector"] = rel(proj_gpu[b], tr["projector.output"].reshape(G * G, -1))
+        assert r["projector"] < 3 * tol, r
         report.append(r)
     print(f"\n{variant}/{dtype}: {report}")
-    eng.close()
-    for r in report:
-        assert r["logits"] < tol and r["boxes"] < tol, r
-        assert r["projector"] < 3 * tol and r["cls_all"] < 3 * tol, r
-        if "masks" in r:
-            assert r["masks"] < 5 * tol and r["mask_sign_agree"] >= 0.99, r
 
 
 def test_rgb_and_planar_paths_agree(make_model):
@@ -122,15 +173,14 @@ def test_nano_batch1_parity(make_model):
     eng = lib.Engine(path)
     img = _images(384, 1, 1000)
     lg, bx, _ = eng.forward_rgb(img)
+    topk = eng.trace("topk", 1).astype(np.int64)
+    cls_gpu = eng.trace("two_stage.cls_all", 1).reshape(-1, 91)
+    eng.close()
     x = ora.preprocess(img[0])
     own = ora.forward(x, trace=True)
-    topk = eng.trace("topk", 1).astype(np.int64)
     cls_o = own["trace"]["two_stage.cls_all"].reshape(-1, 91)
-    check_topk(topk, own["topk"], cls_o.max(1), 1e-3)
-    forced = ora.forward(x, force_topk=topk)
-    assert rel(lg[0], forced["logits"]) < 1e-3
-    assert rel(bx[0], forced["boxes"]) < 1e-3
-    eng.close()
+    r = compare_image(ora, x, lg[0], bx[0], None, topk, cls_gpu, cls_o, own["topk"], 1e-3)
+    print(f"\nnano/f16 batch 1: {r}")
 
 
 def test_graph_replay_matches_direct_launches(make_model, monkeypatch):
@@ -267,9 +317,10 @@ def test_streaming_submissions_wait_oldest(make_model):
 FULL = [("nano", "f16"), ("base", "q8_0"), ("medium", "q4_K"), ("seg-small", "f16"), ("large", "f16")]
 
 
-def _check_variant(variant, dtype, batch, make_model):
+def _check_variant(variant, dtype, batch, make_model, sample=None):
     """Engine vs oracle at the variant's full size: class scores and top-K,
-    then logits / boxes / masks with the oracle forced onto the engine's top-K."""
+    then logits / boxes / masks with the oracle forced onto the engine's top-K.
+    `sample` lists the images of the batch the oracle checks (default: all)."""
     import oracle as O
     from rfdetr_b200 import lib
 
@@ -285,22 +336,31 @@ def _check_variant(variant, dtype, batch, make_model):
     cls_gpu = eng.trace("two_stage.cls_all", batch).reshape(batch, G * G, NC)
     eng.close()
     tol = TOL[dtype]
-    for b in range(batch):
+    report = []
+    for b in (sample if sample is not None else range(batch)):
         x = ora.preprocess(imgs[b])
         own = ora.forward(x, trace=True)
         cls_o = own["trace"]["two_stage.cls_all"].reshape(G * G, NC)
-        assert rel(cls_gpu[b], cls_o) < 3 * tol
-        check_topk(topk[b], own["topk"], cls_o.max(1), tol)
-        forced = ora.forward(x, force_topk=topk[b])
-        assert rel(lg[b], forced["logits"]) < tol, (variant, b, rel(lg[b], forced["logits"]))
-        assert rel(bx[b], forced["boxes"]) < tol, (variant, b)
-        if mk is not None:
-            assert ((mk[b] > 0) == (forced["masks"] > 0)).mean() >= 0.99
+        r = compare_image(ora, x, lg[b], bx[b], None if mk is None else mk[b], topk[b], cls_gpu[b], cls_o,
+                          own["topk"], tol, mode2=dtype in ("q8_0", "q4_K"))
+        r["image"] = b
+        report.append(r)
+    print(f"\n{variant}/{dtype} batch {batch}: {report}")
 
 
 @pytest.mark.parametrize("variant,dtype", FULL)
 def test_full_size_configs(variant, dtype, make_model):
     _check_variant(variant, dtype, 2, make_model)
+
+
+@pytest.mark.parametrize("variant,dtype,batch,sample", [("base", "q8_0", 32, (0, 17, 31)),
+                                                        ("base", "q8_0", 64, (0, 63)),
+                                                        ("large", "f16", 256, (0, 137, 255))])
+def test_benchmarked_batches(variant, dtype, batch, sample, make_model):
+    """The batches the benchmark times (Base Q8_0 at 32 and 64 images, Large F16 at 256), checked
+    against the oracle on sampled images of the full batch: the GEMM tiling, split choices and
+    row counts are those of the timed forward."""
+    _check_variant(variant, dtype, batch, make_model, sample)
 
 
 # The remaining variants of the converter's table (scripts/convert_rfdetr_to_gguf.py:125-205)
@@ -526,3 +586,55 @@ def test_flat_capi_with_png_and_seg_masks(make_model, tmp_path):
     assert L.rfdetr_capi_detect_buffer(h, b"not an image", 12, 0.3, 5, C.byref(out)) != 0
     assert L.rfdetr_capi_get_n_detections(h) == 0
     assert L.rfdetr_capi_unload(h) == 0
+
+
+_FAULT_CHILD = r'''
+import ctypes as C, sys
+import numpy as np
+sys.path.insert(0, sys.argv[2])
+from rfdetr_b200 import lib
+L = lib.lib()
+eng = lib.Engine(sys.argv[1], max_batch=2)
+rng = np.random.default_rng(5)
+arrs = [rng.integers(0, 256, (200, 160, 3), dtype=np.uint8), rng.integers(0, 256, (96, 144, 3), dtype=np.uint8)]
+st = C.c_int(0)
+imgs = [L.rfdetr_image_from_rgb_buffer(a.ctypes.data, a.shape[1], a.shape[0], C.byref(st)) for a in arrs]
+dp = lib.DetectParams(0.0, 5, None, 0)   # threshold 0: every image has detections
+dets = (C.POINTER(lib.Detection) * 2)()
+counts = (C.c_size_t * 2)(7, 7)
+# two runs (two sizes): the first run's post-processing succeeds, the second throws after handing out an array
+rc = L.rfdetr_b200_detect_batch(eng.ctx, (C.c_void_p * 2)(*imgs), 2, C.byref(dp), dets, counts)
+print("batch", rc, bool(dets[0]), bool(dets[1]), list(counts))
+out = C.POINTER(lib.Detection)()
+n = C.c_size_t(9)
+rc1 = L.rfdetr_detect(eng.ctx, imgs[0], C.byref(dp), C.byref(out), C.byref(n))   # third call: no fault
+print("detect", rc1, bool(out), n.value)
+L.rfdetr_detections_free(out, n.value)
+for im in imgs:
+    L.rfdetr_image_free(im)
+eng.close()
+'''
+
+
+def test_postprocess_allocation_failure_releases_every_array(make_model, tmp_path):
+    """An allocation failure thrown while detection arrays are being built (injected on the host:
+    RFDETR_FAULT_INJECT=postprocess_alloc:2 makes the second post-processing call of the process throw
+    std::bad_alloc after its first array is handed out) ends rfdetr_b200_detect_batch with
+    RFDETR_ERR_OUT_OF_MEMORY and every output cleared, the arrays of the run before it included, and
+    the context keeps working (a later rfdetr_detect succeeds).  Runs in a child process so the
+    injection counter starts at zero."""
+    import subprocess
+    import sys
+
+    path = make_model("tiny", "f16", 0)
+    script = tmp_path / "fault_child.py"
+    script.write_text(_FAULT_CHILD)
+    env = dict(os.environ, RFDETR_FAULT_INJECT="postprocess_alloc:2")
+    pkg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "rf-detr.cpp_b200")
+    r = subprocess.run([sys.executable, str(script), path, pkg], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = dict(line.split(" ", 1) for line in r.stdout.strip().splitlines())
+    assert lines["batch"] == "-4 False False [0, 0]", r.stdout   # RFDETR_ERR_OUT_OF_MEMORY
+    rc1, has, n = lines["detect"].split()
+    assert rc1 == "0" and has == "True" and int(n) > 0

@@ -3,12 +3,14 @@ call cudaMalloc (its im2col scratch is a fixed device array inside the
 library instead of a caller workspace).
 
 Checked through the C ABI against rfdetr_b200_op_conv3x3 (the workspace
-variant) on two calls in a row with different inputs, so a second call that
-reused stale scratch contents would be caught.  This file is collected last on
-purpose; it passes alone in a fresh process and after the other tests.
+variant) and directly against a float64 torch conv2d + layer_norm (+ SiLU), on
+two calls in a row with different inputs, so a second call that reused stale
+scratch contents would be caught.  This file is collected last on purpose; it
+passes alone in a fresh process and after the other tests.
 """
 import pytest
 import torch
+import torch.nn.functional as F
 
 pytestmark = pytest.mark.gpu
 
@@ -49,6 +51,13 @@ def test_noalloc_conv3x3_matches_workspace_variant():
         assert torch.isfinite(out32).all() and torch.isfinite(out16.float()).all()
         assert rel(out32, ref32) < 1e-6, call
         assert rel(out16, ref16) < 1e-3, call
+        # the same ConvX block in float64: 3x3 convolution, channel LayerNorm (eps 1e-6), SiLU
+        xd = x.double().reshape(B, H, W, C).permute(0, 3, 1, 2)
+        wd = w.double().permute(0, 3, 1, 2)  # [oc][ky][kx][c] -> [oc][c][ky][kx]
+        y = F.conv2d(xd, wd, padding=1).permute(0, 2, 3, 1)
+        y = F.silu(F.layer_norm(y, (OC,), g.double(), b.double(), 1e-6)).reshape(-1, OC)
+        assert rel(out32, y) < 1e-4, call
+        assert rel(out16, y) < 2e-3, call
 
 
 def test_noalloc_conv3x3_rejects_oversize():
