@@ -1,14 +1,19 @@
-// Image I/O for the public API: rfdetr_image objects, decoding (PNG via zlib,
-// binary PPM, JPEG via nvJPEG on the GPU) and PNG encoding (grayscale masks
-// for the flat C API, RGB for rfdetr_render).  Behaviour of the reference's
-// src/image_io.cpp (stb-based) at the API level: images are 8-bit RGB, HWC.
+// Image I/O for the public API: rfdetr_image objects, decoding and PNG encoding
+// (grayscale masks for the flat C API, RGB for rfdetr_render).  Behaviour of the
+// reference's src/image_io.cpp at the API level: images are 8-bit RGB, HWC.
+// Decoding: PNG (non-interlaced, via zlib) and binary PPM here (lossless, so the
+// same pixels as any decoder); JPEG and every other format through stb_image, the
+// decoder the reference links (stb_decode.cc), so the pixels are the reference's
+// byte for byte; nvJPEG only when the library was built without stb_image.
 #include "image_io.hpp"
 
 #include "common.hpp"
+#include "stb_decode.hpp"
 
 #include <nvjpeg.h>
 #include <zlib.h>
 
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -167,8 +172,26 @@ bool decode_ppm(const uint8_t* d, size_t n, int* w, int* h, std::vector<uint8_t>
     return true;
 }
 
-// ---- JPEG via nvJPEG (device decode, copied back to host)
-bool decode_jpeg(const uint8_t* d, size_t n, int* w, int* h, std::vector<uint8_t>& rgb) {
+// ---- stb_image (JPEG, interlaced PNG, BMP, GIF, TGA, PSD, HDR, PIC): the reference's decoder
+bool decode_stb(const uint8_t* d, size_t n, int* w, int* h, std::vector<uint8_t>& rgb) {
+    if (!rfb_stb_available() || n > (size_t)INT32_MAX) return false;
+    int W = 0, H = 0;
+    unsigned char* px = rfb_stb_decode_rgb(d, (int)n, &W, &H);
+    if (!px) return false;
+    struct Free {
+        unsigned char* p;
+        ~Free() { rfb_stb_free(p); }
+    } guard{px};
+    rgb.assign(px, px + (size_t)W * (size_t)H * 3);  // std::bad_alloc is handled by the caller
+    *w = W;
+    *h = H;
+    return true;
+}
+
+// ---- JPEG via nvJPEG (device decode, copied back to host): only without stb_image; its IDCT and
+// chroma upsampling are not stb's, so the pixels can differ from the reference's by a few levels
+bool decode_jpeg_nvjpeg(const uint8_t* d, size_t n, int* w, int* h, std::vector<uint8_t>& rgb) {
+    if (rfb_stb_available()) return false;
     if (n < 3 || d[0] != 0xFF || d[1] != 0xD8) return false;
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
@@ -257,14 +280,15 @@ extern "C" rfdetr_image* rfdetr_image_load_buffer(const uint8_t* bytes, size_t l
     bool ok = false;
     try {
         ok = decode_png(bytes, len, &w, &h, img->rgb) || decode_ppm(bytes, len, &w, &h, img->rgb) ||
-             decode_jpeg(bytes, len, &w, &h, img->rgb);
+             decode_stb(bytes, len, &w, &h, img->rgb) || decode_jpeg_nvjpeg(bytes, len, &w, &h, img->rgb);
     } catch (const std::bad_alloc&) {
         delete img;
         set(RFDETR_ERR_OUT_OF_MEMORY);
         return nullptr;
     }
     if (!ok) {
-        rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_image_load_buffer: unsupported or corrupt image (%zu bytes)", len);
+        rfdetr_logf(RFDETR_LOG_ERROR, "rfdetr_image_load_buffer: unsupported or corrupt image (%zu bytes): %s", len,
+                    rfb_stb_reason());
         delete img;
         set(RFDETR_ERR_DECODE);
         return nullptr;
@@ -301,15 +325,19 @@ extern "C" rfdetr_image* rfdetr_image_load_file(const char* path, rfdetr_status*
 extern "C" rfdetr_image* rfdetr_image_from_rgb_buffer(const uint8_t* rgb, int width, int height, rfdetr_status* st) {
     auto set = [&](rfdetr_status s) { if (st) *st = s; };
     if (!rgb || width <= 0 || height <= 0) { set(RFDETR_ERR_INVALID_ARG); return nullptr; }
+    // more bytes than a buffer can hold: not a real image (checked before rgb + bytes is formed,
+    // which would itself be undefined for such a size)
+    const size_t bytes = (size_t)width * (size_t)height * 3;
+    if (bytes > (size_t)PTRDIFF_MAX / 2) { set(RFDETR_ERR_INVALID_ARG); return nullptr; }
     auto* img = new (std::nothrow) rfdetr_image();
     if (!img) { set(RFDETR_ERR_OUT_OF_MEMORY); return nullptr; }
     try {
-        img->rgb.assign(rgb, rgb + (size_t)width * height * 3);
+        img->rgb.assign(rgb, rgb + bytes);
     } catch (const std::bad_alloc&) {
         delete img;
         set(RFDETR_ERR_OUT_OF_MEMORY);
         return nullptr;
-    } catch (const std::length_error&) {  // more bytes than a buffer can hold: not a real image
+    } catch (const std::length_error&) {
         delete img;
         set(RFDETR_ERR_INVALID_ARG);
         return nullptr;
