@@ -226,18 +226,6 @@ int rfdetr_b200_op_mask_bits(const float* d_masks, int batch, int nq, int side, 
 int rfdetr_b200_op_deform(const void* value, const float* so_aw, int ld_soaw, const float* refp, int batch, int nq,
                           int grid, int heads, int points, int dm, void* out, void* stream);
 
-/* Deformable cross-attention sampling with its two input linears fused in
- * (src/decoder.cpp:238-259 sampling_offsets and attention_weights, then
- * def_attn_op :127-207): so_aw = q . W^T + bias per query (q f16 [batch*nq]
- * [ldq]; W f16 [heads*points*3][ldw] = the offsets linear's rows followed by the
- * attention-weights linear's; bias f32 [heads*points*3]), then the sampling of
- * rfdetr_b200_op_deform from that row.  Requires heads*points*3 == 96 (16
- * heads x 2 points), dm a multiple of 16 up to 512 and 16-byte aligned value,
- * W and out; cudaErrorInvalidValue otherwise, before any launch. */
-int rfdetr_b200_op_deform_fused(const void* value, const void* q, int ldq, const void* w, int ldw, const float* bias,
-                                const float* refp, int batch, int nq, int grid, int heads, int points, int dm,
-                                void* out, void* stream);
-
 /* 3x3 convolution, stride 1, zero padding 1, no bias, over channels-last f16
  * maps (`src` rows = batch*h*w pixels, `c` channels at pitch `lds`), followed
  * by a LayerNorm over the `oc` output channels (oc = 128 or 256) and an

@@ -723,19 +723,12 @@ rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int 
                tgt_, Dm);
         L.check(add_to_f16(tgt_, qpos_, (size_t)Mq * Dm, qk16_, st), "x+pos");
         L.gemm("value_proj", mem16_, Dm, Mp, Ly.value, EPI_F16, ACT_NONE, nullptr, 0, value_, Dm);
-        {
-            // sampling offsets + attention weights (src/decoder.cpp:238-259) and the bilinear gather
-            // (:127-207): one kernel when the stacked linears have 96 outputs (16 heads x 2 points)
-            const int ch = (int)cfg_.decoder.cross_attn_heads, cp = (int)cfg_.decoder.cross_attn_n_points;
-            if (n_soaw_ == 96 && Dm % 16 == 0 && Dm <= 512) {
-                L.check(deform_fused(value_, qk16_, Dm, Ly.soaw.w, Ly.soaw.ldw, Ly.soaw.b, refp_, B, NQ, G, ch, cp, Dm,
-                                     samp_, st),
-                        "deform");
-            } else {
-                L.gemm("so_aw", qk16_, Dm, Mq, Ly.soaw, EPI_F32, ACT_NONE, soaw_, n_soaw_, nullptr, 0);
-                L.check(deform_sample(value_, soaw_, n_soaw_, refp_, B, NQ, G, ch, cp, Dm, samp_, st), "deform");
-            }
-        }
+        // sampling offsets + attention weights (src/decoder.cpp:238-259) as one N = 96 GEMM, then the
+        // bilinear gather (:127-207)
+        L.gemm("so_aw", qk16_, Dm, Mq, Ly.soaw, EPI_F32, ACT_NONE, soaw_, n_soaw_, nullptr, 0);
+        L.check(deform_sample(value_, soaw_, n_soaw_, refp_, B, NQ, G, (int)cfg_.decoder.cross_attn_heads,
+                              (int)cfg_.decoder.cross_attn_n_points, Dm, samp_, st),
+                "deform");
         L.gemm("ca.out+norm2", samp_, Dm, Mq, Ly.oproj, EPI_LN, ACT_NONE, tgt_, Dm, tgt16_, Dm, nullptr, &Ly.n2, 1e-5f,
                tgt_, Dm);
         L.gemm("linear1", tgt16_, Dm, Mq, Ly.l1, EPI_F16, ACT_RELU, nullptr, 0, ffn_, Fd_);

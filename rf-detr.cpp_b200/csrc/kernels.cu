@@ -6,8 +6,6 @@
 #include "kernels.cuh"
 
 #include <cuda_fp16.h>
-
-#include <atomic>
 #include <stdint.h>
 
 namespace rfb {
@@ -685,8 +683,14 @@ __global__ void k_to_f16(const float* __restrict__ a, size_t n, __half* __restri
 // One warp per query; each lane owns 8 consecutive channels (16 bytes of f16
 // value per corner), 2 lanes per 16-channel head.  `row` holds the query's
 // sampling offsets (H*P*2) then attention logits (H*P); vb is its image's value map.
+// PP > 0: the point count as a compile-time constant, so the loads of every (point, corner) of the
+// lane's 8 channels are issued before any of them is used (one memory latency per query instead of
+// one per corner); PP == 0: any count P at run time.  Same arithmetic either way (an out-of-map
+// corner contributes nothing).
+template <int PP>
 __device__ __forceinline__ void deform_query(const __half* __restrict__ vb, const float* row, const float* rp,
-                                             int G, int H, int P, int Dm, int lane, __half* __restrict__ orow) {
+                                             int G, int H, int P_rt, int Dm, int lane, __half* __restrict__ orow) {
+    const int P = PP > 0 ? PP : P_rt;
     const int hd = Dm / H;
     const float r0 = rp[0], r1 = rp[1], r2 = rp[2], r3 = rp[3];
     const float off_scale = 0.5f / (float)P;
@@ -701,33 +705,47 @@ __device__ __forceinline__ void deform_query(const __half* __restrict__ vb, cons
         float acc[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-        for (int p = 0; p < P; ++p) {
-            const float wa = expf(row[H * P * 2 + h * P + p] - mx) * inv;
-            const float sx = (row[(h * P + p) * 2 + 0] * off_scale) * r2 + r0;
-            const float sy = (row[(h * P + p) * 2 + 1] * off_scale) * r3 + r1;
-            const float ix = sx * (float)G - 0.5f, iy = sy * (float)G - 0.5f;
-            const int ix0 = (int)floorf(ix), iy0 = (int)floorf(iy);
-            const float wx1 = ix - (float)ix0, wy1 = iy - (float)iy0;
-            const float wx0 = 1.f - wx1, wy0 = 1.f - wy1;
-            float s[8];
+        constexpr int NP = PP > 0 ? PP : 1;  // points whose corners are loaded together
+        for (int p0 = 0; p0 < P; p0 += NP) {
+            uint4 u[NP][4];
+            float wc[NP][4], wa[NP];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) s[e] = 0.f;
+            for (int k = 0; k < NP; ++k) {
+                const int p = p0 + k;
+                wa[k] = expf(row[H * P * 2 + h * P + p] - mx) * inv;
+                const float sx = (row[(h * P + p) * 2 + 0] * off_scale) * r2 + r0;
+                const float sy = (row[(h * P + p) * 2 + 1] * off_scale) * r3 + r1;
+                const float ix = sx * (float)G - 0.5f, iy = sy * (float)G - 0.5f;
+                const int ix0 = (int)floorf(ix), iy0 = (int)floorf(iy);
+                const float wx1 = ix - (float)ix0, wy1 = iy - (float)iy0;
+                const float wx0 = 1.f - wx1, wy0 = 1.f - wy1;
 #pragma unroll
-            for (int corner = 0; corner < 4; ++corner) {
-                const int xi = ix0 + (corner & 1), yi = iy0 + (corner >> 1);
-                if (xi < 0 || xi >= G || yi < 0 || yi >= G) continue;
-                const float wgt = ((corner & 1) ? wx1 : wx0) * ((corner >> 1) ? wy1 : wy0);
-                const uint4 u = *reinterpret_cast<const uint4*>(vb + ((size_t)yi * G + xi) * Dm + c * 8);
-                const __half2* h2 = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(h2[e]);
-                    s[2 * e] += wgt * f.x;
-                    s[2 * e + 1] += wgt * f.y;
+                for (int corner = 0; corner < 4; ++corner) {
+                    const int xi = ix0 + (corner & 1), yi = iy0 + (corner >> 1);
+                    const bool in = xi >= 0 && xi < G && yi >= 0 && yi < G;
+                    wc[k][corner] = ((corner & 1) ? wx1 : wx0) * ((corner >> 1) ? wy1 : wy0);
+                    u[k][corner] = in ? __ldg(reinterpret_cast<const uint4*>(vb + ((size_t)yi * G + xi) * Dm + c * 8))
+                                      : make_uint4(0u, 0u, 0u, 0u);
                 }
             }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] += wa * s[e];
+            for (int k = 0; k < NP; ++k) {
+                float s[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) s[e] = 0.f;
+#pragma unroll
+                for (int corner = 0; corner < 4; ++corner) {
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&u[k][corner]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(h2[e]);
+                        s[2 * e] += wc[k][corner] * f.x;
+                        s[2 * e + 1] += wc[k][corner] * f.y;
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] += wa[k] * s[e];
+            }
         }
         uint4 o;
         __half2* oh = reinterpret_cast<__half2*>(&o);
@@ -745,95 +763,12 @@ __global__ void k_deform(const __half* __restrict__ value, const float* __restri
     const int lane = threadIdx.x & 31;
     if (bq >= B * NQ) return;
     const int b = bq / NQ;
-    deform_query(value + (size_t)b * G * G * Dm, so_aw + (size_t)bq * ld_soaw, refp + (size_t)bq * 4, G, H, P, Dm,
-                 lane, out + (size_t)bq * Dm);
-}
-
-// The sampling-offset and attention-weight linears (src/decoder.cpp:238-259) fused in front of the
-// gather: so_aw = q . W^T + bias with W f16 [NS][K] (NS = H*P*3 outputs, the two linears stacked),
-// q f16 [B*NQ][ldq].  Each warp takes 16 queries: their NS values come from mma.sync m16n8k16 (f16
-// operands, f32 accumulation; W staged once per CTA in shared memory), land in a per-warp shared
-// tile, and each query's gather reads its row there.  Persistent CTAs loop over the 16-query tiles.
-constexpr int kDefWarps = 4;
-__host__ __device__ constexpr int deform_w_pitch(int K) { return K + 8; }  // halfs: 16-byte pad spreads banks
-__host__ __device__ constexpr int deform_so_pitch(int NS) { return NS + 4; }
-
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-template <int NS>
-__global__ void __launch_bounds__(32 * kDefWarps) k_deform_fused(const __half* __restrict__ value,
-                                                                 const __half* __restrict__ q, int ldq,
-                                                                 const __half* __restrict__ w, int ldw,
-                                                                 const float* __restrict__ bias,
-                                                                 const float* __restrict__ refp, int B, int NQ,
-                                                                 int G, int H, int P, int Dm,
-                                                                 __half* __restrict__ out) {
-    extern __shared__ __align__(16) uint8_t dsm[];
-    const int K = Dm;
-    const int wp = deform_w_pitch(K);
-    __half* sw = reinterpret_cast<__half*>(dsm);                                    // [NS][wp]
-    float* sbias = reinterpret_cast<float*>(dsm + (size_t)NS * wp * 2);             // [NS]
-    float* sso = sbias + NS;                                                         // [warps][16][so pitch]
-    constexpr int SOP = deform_so_pitch(NS);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // stage W and the bias (16-byte copies; K is a multiple of 16)
-    const int chunks = K / 8;
-    for (int i = threadIdx.x; i < NS * chunks; i += blockDim.x) {
-        const int r = i / chunks, c = i - r * chunks;
-        *reinterpret_cast<uint4*>(sw + (size_t)r * wp + c * 8) =
-            *reinterpret_cast<const uint4*>(w + (size_t)r * ldw + c * 8);
-    }
-    for (int i = threadIdx.x; i < NS; i += blockDim.x) sbias[i] = bias ? bias[i] : 0.f;
-    __syncthreads();
-    float* so = sso + (size_t)warp * 16 * SOP;
-    const int rows = B * NQ;
-    const int tiles = (rows + 15) / 16;
-    const int g = lane >> 2, t4 = lane & 3;
-    for (int tile = blockIdx.x * kDefWarps + warp; tile < tiles; tile += gridDim.x * kDefWarps) {
-        const int r0 = tile * 16;
-        const int ra = r0 + g, rb = r0 + g + 8;
-        const __half* qa = q + (size_t)(ra < rows ? ra : 0) * ldq;
-        const __half* qb = q + (size_t)(rb < rows ? rb : 0) * ldq;
-        float acc[NS / 8][4];
-#pragma unroll
-        for (int n = 0; n < NS / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-        for (int k0 = 0; k0 < K; k0 += 16) {
-            const int kc = k0 + 2 * t4;
-            uint32_t a[4];
-            a[0] = ra < rows ? *reinterpret_cast<const uint32_t*>(qa + kc) : 0u;
-            a[1] = rb < rows ? *reinterpret_cast<const uint32_t*>(qb + kc) : 0u;
-            a[2] = ra < rows ? *reinterpret_cast<const uint32_t*>(qa + kc + 8) : 0u;
-            a[3] = rb < rows ? *reinterpret_cast<const uint32_t*>(qb + kc + 8) : 0u;
-#pragma unroll
-            for (int n = 0; n < NS / 8; ++n) {
-                const __half* wr = sw + (size_t)(n * 8 + g) * wp + kc;
-                mma_16816(acc[n], a, *reinterpret_cast<const uint32_t*>(wr), *reinterpret_cast<const uint32_t*>(wr + 8));
-            }
-        }
-#pragma unroll
-        for (int n = 0; n < NS / 8; ++n) {
-            const int c = n * 8 + 2 * t4;
-            so[g * SOP + c] = acc[n][0] + sbias[c];
-            so[g * SOP + c + 1] = acc[n][1] + sbias[c + 1];
-            so[(g + 8) * SOP + c] = acc[n][2] + sbias[c];
-            so[(g + 8) * SOP + c + 1] = acc[n][3] + sbias[c + 1];
-        }
-        __syncwarp();
-        const int nr = rows - r0 < 16 ? rows - r0 : 16;
-        for (int i = 0; i < nr; ++i) {
-            const int bq = r0 + i;
-            const int b = bq / NQ;
-            deform_query(value + (size_t)b * G * G * Dm, so + i * SOP, refp + (size_t)bq * 4, G, H, P, Dm, lane,
-                         out + (size_t)bq * Dm);
-        }
-        __syncwarp();  // the tile's rows are read before the next tile overwrites them
-    }
+    if (P == 2)  // the converter's variants: loads of both points issued together
+        deform_query<2>(value + (size_t)b * G * G * Dm, so_aw + (size_t)bq * ld_soaw, refp + (size_t)bq * 4, G, H, P,
+                        Dm, lane, out + (size_t)bq * Dm);
+    else
+        deform_query<0>(value + (size_t)b * G * G * Dm, so_aw + (size_t)bq * ld_soaw, refp + (size_t)bq * 4, G, H, P,
+                        Dm, lane, out + (size_t)bq * Dm);
 }
 
 // src/rfdetr_model.cpp:438-448
@@ -1146,38 +1081,6 @@ cudaError_t deform_sample(const __half* value, const float* so_aw, int ld_soaw, 
                           int G, int heads, int points, int Dm, __half* out, cudaStream_t st) {
     if (Dm % 8 || (Dm / heads) % 8) return cudaErrorInvalidValue;
     k_deform<<<cdiv((size_t)B * NQ, 4), 128, 0, st>>>(value, so_aw, ld_soaw, refp, B, NQ, G, heads, points, Dm, out);
-    return cudaGetLastError();
-}
-
-size_t deform_fused_smem(int ns, int dm) {
-    return (size_t)ns * deform_w_pitch(dm) * 2 + (size_t)ns * 4 + (size_t)kDefWarps * 16 * deform_so_pitch(ns) * 4;
-}
-
-cudaError_t deform_fused(const __half* value, const __half* q, int ldq, const __half* w, int ldw, const float* bias,
-                         const float* refp, int B, int NQ, int G, int heads, int points, int Dm, __half* out,
-                         cudaStream_t st) {
-    const int ns = heads * points * 3;
-    if (!value || !q || !w || !refp || !out || B <= 0 || NQ <= 0 || G <= 0 || heads <= 0 || points <= 0)
-        return cudaErrorInvalidValue;
-    if (Dm % 16 || Dm > 512 || (Dm / heads) % 8 || Dm % heads || ns != 96 || ldq % 2 || ldw % 8 || ldq < Dm ||
-        ldw < Dm || ((uintptr_t)q & 3) || ((uintptr_t)w & 15) || ((uintptr_t)value & 15) || ((uintptr_t)out & 15))
-        return cudaErrorInvalidValue;
-    const size_t smem = deform_fused_smem(ns, Dm);
-    static std::atomic<uint64_t> attr_set{0};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (!(attr_set.load() & (1ull << (dev & 63)))) {
-        e = cudaFuncSetAttribute(k_deform_fused<96>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_set.fetch_or(1ull << (dev & 63));
-    }
-    if (smem > 100 * 1024) return cudaErrorInvalidValue;
-    const unsigned tiles = cdiv((size_t)B * NQ, 16);
-    const unsigned ctas = cdiv(tiles, kDefWarps);
-    const unsigned grid = ctas < 148u * 2u ? ctas : 148u * 2u;
-    k_deform_fused<96><<<grid, 32 * kDefWarps, smem, st>>>(value, q, ldq, w, ldw, bias, refp, B, NQ, G, heads,
-                                                           points, Dm, out);
     return cudaGetLastError();
 }
 

@@ -92,13 +92,6 @@ cudaError_t to_f16(const float* a, size_t n, __half* out, cudaStream_t st);
 cudaError_t deform_sample(const __half* value, const float* so_aw, int ld_soaw, const float* refp, int B, int NQ,
                           int G, int heads, int points, int Dm, __half* out, cudaStream_t st);
 
-// The same with the sampling-offset / attention-weight linears fused in front of the gather:
-// so_aw = q . W^T + bias computed in the kernel (q f16 [B*NQ][ldq], W f16 [H*P*3][ldw] = the two
-// linears stacked, offsets first, bias f32 [H*P*3]).  Needs H*P*3 == 96, Dm a multiple of 16
-// (<= 512) and 16-byte aligned value / W / out; cudaErrorInvalidValue otherwise, before any launch.
-cudaError_t deform_fused(const __half* value, const __half* q, int ldq, const __half* w, int ldw, const float* bias,
-                         const float* refp, int B, int NQ, int G, int heads, int points, int Dm, __half* out,
-                         cudaStream_t st);
 
 // Final boxes: delta [B*NQ][4] with refpoints -> cxcywh [B*NQ][4].
 cudaError_t box_reparam(const float* delta, const float* refp, int n, float* out, cudaStream_t st);

@@ -105,14 +105,6 @@ extern "C" int rfdetr_b200_op_deform(const void* value, const float* so_aw, int 
                                    points, dm, static_cast<__half*>(out), static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int rfdetr_b200_op_deform_fused(const void* value, const void* q, int ldq, const void* w, int ldw,
-                                           const float* bias, const float* refp, int batch, int nq, int grid,
-                                           int heads, int points, int dm, void* out, void* stream) {
-    return (int)rfb::deform_fused(static_cast<const __half*>(value), static_cast<const __half*>(q), ldq,
-                                  static_cast<const __half*>(w), ldw, bias, refp, batch, nq, grid, heads, points, dm,
-                                  static_cast<__half*>(out), static_cast<cudaStream_t>(stream));
-}
-
 extern "C" size_t rfdetr_b200_op_conv3x3_workspace(int batch, int h, int w, int c) {
     if (batch <= 0 || h <= 0 || w <= 0 || c <= 0) return 0;
     return (size_t)batch * h * w * 9 * c * sizeof(__half);

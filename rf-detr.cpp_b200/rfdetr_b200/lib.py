@@ -133,9 +133,6 @@ SIGNATURES = {
     "rfdetr_b200_mask_bits_words": (C.c_size_t, [C.c_int, C.c_int]),
     "rfdetr_b200_op_mask_bits": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                            C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
-    "rfdetr_b200_op_deform_fused": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
-                                              C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
-                                              C.c_void_p, C.c_void_p]),
     "rfdetr_b200_op_deform": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                         C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "rfdetr_b200_op_conv3x3_workspace": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
