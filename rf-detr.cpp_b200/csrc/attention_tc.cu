@@ -63,6 +63,13 @@ struct AttnCfg {
     static constexpr int MIN_CTAS = NS == 2 ? 3 : 2;
 };
 
+// max of three floats in one instruction (sm_100): the row max takes one per two scores
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -231,7 +238,7 @@ k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
                     r0[e] = __float_as_uint(x0);
                     r1[e] = __float_as_uint(x1);
                 }
-                mx4[e & 3] = fmaxf(mx4[e & 3], fmaxf(x0, x1));
+                mx4[e & 3] = fmax3(mx4[e & 3], x0, x1);
             }
             // scale > 0 commutes with max; running max in log2 units
             const float m_cand = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2);
@@ -488,7 +495,7 @@ k_attn_tc_items(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                         r0[e] = __float_as_uint(x0);
                         r1[e] = __float_as_uint(x1);
                     }
-                    mx4[e & 3] = fmaxf(mx4[e & 3], fmaxf(x0, x1));
+                    mx4[e & 3] = fmax3(mx4[e & 3], x0, x1);
                 }
                 const float m_cand = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2);
                 const float m_new = m_cand > m + kRescaleLog2 ? m_cand : m;
