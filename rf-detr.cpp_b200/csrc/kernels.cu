@@ -679,6 +679,17 @@ __global__ void k_to_f16(const float* __restrict__ a, size_t n, __half* __restri
     if (i < n) out[i] = __float2half_rn(a[i]);
 }
 
+// 8 values per thread: two 16-byte loads, one 16-byte store (grid-strided)
+__global__ void k_to_f16_v8(const float4* __restrict__ a, size_t n8, uint4* __restrict__ out) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 u = a[2 * i], v = a[2 * i + 1];
+        const __half2 h0 = __floats2half2_rn(u.x, u.y), h1 = __floats2half2_rn(u.z, u.w);
+        const __half2 h2 = __floats2half2_rn(v.x, v.y), h3 = __floats2half2_rn(v.z, v.w);
+        out[i] = make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                            *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+    }
+}
+
 // ---- deformable sampling: src/decoder.cpp:127-207, 236-285 ------------------
 // One warp per query; each lane owns 8 consecutive channels (16 bytes of f16
 // value per corner), 2 lanes per 16-channel head.  `row` holds the query's
@@ -808,6 +819,125 @@ __global__ void k_resize_bilinear(const float* __restrict__ src, int B, int G, i
     const float a = s[((size_t)y0 * G + x0) * C], bb = s[((size_t)y0 * G + x1) * C];
     const float cc = s[((size_t)y1 * G + x0) * C], d = s[((size_t)y1 * G + x1) * C];
     dst[i] = a * (1 - dx) * (1 - dy) + bb * dx * (1 - dy) + cc * (1 - dx) * dy + d * dx * dy;
+}
+
+// Bilinear resize (align_corners = False, clamped edges), 4 channels per thread with 16-byte loads and
+// stores and 32-bit index arithmetic; the same per-element arithmetic as k_resize_bilinear.
+__global__ void k_resize_bilinear4(const float* __restrict__ src, int B, int G, int T, int C, float* __restrict__ dst) {
+    const int C4 = C >> 2;
+    const unsigned n = (unsigned)B * T * T * C4;
+    const float sf = (float)T / (float)G;
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const unsigned c4 = i % (unsigned)C4;
+        const unsigned pix = i / (unsigned)C4;
+        const unsigned b = pix / (unsigned)(T * T);
+        const unsigned r = pix - b * (unsigned)(T * T);
+        const int yy = (int)(r / (unsigned)T), xx = (int)(r - (r / (unsigned)T) * (unsigned)T);
+        const float fy = ((float)yy + 0.5f) / sf - 0.5f;
+        int y0 = (int)floorf(fy), y1 = y0 + 1;
+        y0 = min(max(y0, 0), G - 1);
+        y1 = min(max(y1, 0), G - 1);
+        const float dy = fminf(fmaxf(fy - (float)y0, 0.f), 1.f);
+        const float fx = ((float)xx + 0.5f) / sf - 0.5f;
+        int x0 = (int)floorf(fx), x1 = x0 + 1;
+        x0 = min(max(x0, 0), G - 1);
+        x1 = min(max(x1, 0), G - 1);
+        const float dx = fminf(fmaxf(fx - (float)x0, 0.f), 1.f);
+        const float4* s = reinterpret_cast<const float4*>(src + (size_t)b * G * G * C) + c4;
+        const float4 a = s[((size_t)y0 * G + x0) * C4], bq = s[((size_t)y0 * G + x1) * C4];
+        const float4 cq = s[((size_t)y1 * G + x0) * C4], d = s[((size_t)y1 * G + x1) * C4];
+        float4 o;
+        o.x = a.x * (1 - dx) * (1 - dy) + bq.x * dx * (1 - dy) + cq.x * (1 - dx) * dy + d.x * dx * dy;
+        o.y = a.y * (1 - dx) * (1 - dy) + bq.y * dx * (1 - dy) + cq.y * (1 - dx) * dy + d.y * dx * dy;
+        o.z = a.z * (1 - dx) * (1 - dy) + bq.z * dx * (1 - dy) + cq.z * (1 - dx) * dy + d.z * dx * dy;
+        o.w = a.w * (1 - dx) * (1 - dy) + bq.w * dx * (1 - dy) + cq.w * (1 - dx) * dy + d.w * dx * dy;
+        reinterpret_cast<float4*>(dst)[i] = o;
+    }
+}
+
+// Depthwise 3x3 + bias + channel LN of 256-channel maps (src/segmentation.cpp:68-92), bandwidth-shaped:
+// warp per pixel (warps of a CTA on consecutive pixels, so neighbours are L1 hits), lane per 8
+// consecutive channels (two 16-byte loads per tap, one 16-byte f16 store), the taps' weights
+// transposed tap-major into shared memory once per CTA, the loads of all nine taps issued before
+// their sums (an out-of-map tap reads an in-map pixel and adds it with weight 0): one memory
+// latency per pixel.  Per channel the same sequence of multiply-adds as k_dwconv_ln; the LayerNorm
+// sums run in another order.
+__global__ void __launch_bounds__(256, 2) k_dwconv_ln256(const float* __restrict__ x, int B, int H, int W,
+                                                         const float* __restrict__ w9,
+                                                         const float* __restrict__ bias,
+                                                         const float* __restrict__ g,
+                                                         const float* __restrict__ bb, float eps,
+                                                         __half* __restrict__ out) {
+    constexpr int C = 256;
+    __shared__ __align__(16) float sw[9 * C];  // [tap][channel]
+    __shared__ __align__(16) float sp[3 * C];  // bias, gamma, beta
+    for (int i = threadIdx.x; i < 9 * C; i += blockDim.x) {
+        const int k = i / C, c = i - k * C;
+        sw[i] = w9[c * 9 + k];
+    }
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+        sp[i] = bias[i];
+        sp[C + i] = g[i];
+        sp[2 * C + i] = bb[i];
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c0 = lane * 8;
+    const int npix = B * H * W;
+    for (int pix = blockIdx.x * (blockDim.x >> 5) + warp; pix < npix; pix += gridDim.x * (blockDim.x >> 5)) {
+        const int b = pix / (H * W), r = pix - b * (H * W);
+        const int y = r / W, xq = r - y * W;
+        float4 u[9][2];
+        float wm[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) {
+            const int sy = y + k / 3 - 1, sx = xq + k % 3 - 1;
+            const bool in = sy >= 0 && sy < H && sx >= 0 && sx < W;
+            const float4* src =
+                reinterpret_cast<const float4*>(x + ((size_t)(b * H + (in ? sy : y)) * W + (in ? sx : xq)) * C + c0);
+            u[k][0] = src[0];
+            u[k][1] = src[1];
+            wm[k] = in ? 1.f : 0.f;
+        }
+        float acc[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 9; ++k) {
+            const float4 w0 = *reinterpret_cast<const float4*>(sw + k * C + c0);
+            const float4 w1 = *reinterpret_cast<const float4*>(sw + k * C + c0 + 4);
+            acc[0] += (w0.x * wm[k]) * u[k][0].x;
+            acc[1] += (w0.y * wm[k]) * u[k][0].y;
+            acc[2] += (w0.z * wm[k]) * u[k][0].z;
+            acc[3] += (w0.w * wm[k]) * u[k][0].w;
+            acc[4] += (w1.x * wm[k]) * u[k][1].x;
+            acc[5] += (w1.y * wm[k]) * u[k][1].y;
+            acc[6] += (w1.z * wm[k]) * u[k][1].z;
+            acc[7] += (w1.w * wm[k]) * u[k][1].w;
+        }
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            acc[e] += sp[c0 + e];
+            s += acc[e];
+        }
+        const float mean = warp_sum(s) / (float)C;
+        float q = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float d = acc[e] - mean;
+            q += d * d;
+        }
+        const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)C + eps);
+        uint32_t h[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            const __half2 hv = __floats2half2_rn((acc[e] - mean) * rstd * sp[C + c0 + e] + sp[2 * C + c0 + e],
+                                                 (acc[e + 1] - mean) * rstd * sp[C + c0 + e + 1] + sp[2 * C + c0 + e + 1]);
+            h[e / 2] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        *reinterpret_cast<uint4*>(out + (size_t)pix * C + c0) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
 }
 
 // depthwise 3x3 + bias + channel LN (src/segmentation.cpp:68-92); warp per pixel
@@ -1073,6 +1203,12 @@ cudaError_t add_to_f16(const float* a, const float* b, size_t n, __half* out, cu
 }
 
 cudaError_t to_f16(const float* a, size_t n, __half* out, cudaStream_t st) {
+    if (n % 8 == 0 && !((uintptr_t)a & 15) && !((uintptr_t)out & 15)) {
+        const size_t n8 = n / 8;
+        const unsigned blocks = cdiv(n8, 256) < 148u * 16u ? cdiv(n8, 256) : 148u * 16u;
+        if (n8) k_to_f16_v8<<<blocks, 256, 0, st>>>(reinterpret_cast<const float4*>(a), n8, reinterpret_cast<uint4*>(out));
+        return cudaGetLastError();
+    }
     k_to_f16<<<cdiv(n, 256), 256, 0, st>>>(a, n, out);
     return cudaGetLastError();
 }
@@ -1091,6 +1227,11 @@ cudaError_t box_reparam(const float* delta, const float* refp, int n, float* out
 
 cudaError_t resize_bilinear(const float* src, int B, int G, int T, int C, float* dst, cudaStream_t st) {
     const size_t n = (size_t)B * T * T * C;
+    if (C % 4 == 0 && n / 4 < (1ull << 32) && !((uintptr_t)src & 15) && !((uintptr_t)dst & 15)) {
+        const unsigned blocks = cdiv(n / 4, 256) < 148u * 16u ? cdiv(n / 4, 256) : 148u * 16u;
+        if (n) k_resize_bilinear4<<<blocks, 256, 0, st>>>(src, B, G, T, C, dst);
+        return cudaGetLastError();
+    }
     k_resize_bilinear<<<cdiv(n, 256), 256, 0, st>>>(src, B, G, T, C, dst);
     return cudaGetLastError();
 }
@@ -1098,7 +1239,13 @@ cudaError_t resize_bilinear(const float* src, int B, int G, int T, int C, float*
 cudaError_t dwconv_ln(const float* x, int B, int H, int W, int C, const float* w9, const float* bias,
                       const float* g, const float* b, float eps, __half* out, cudaStream_t st) {
     if (C > 256) return cudaErrorInvalidValue;
-    k_dwconv_ln<<<cdiv((size_t)B * H * W, 8), 256, 0, st>>>(x, B, H, W, C, w9, bias, g, b, eps, out);
+    const size_t npix = (size_t)B * H * W;
+    if (C == 256 && npix < (1u << 30) && !((uintptr_t)x & 15) && !((uintptr_t)out & 15)) {
+        const unsigned blocks = cdiv(npix, 8) < 148u * 8u ? cdiv(npix, 8) : 148u * 8u;
+        if (npix) k_dwconv_ln256<<<blocks, 256, 0, st>>>(x, B, H, W, w9, bias, g, b, eps, out);
+        return cudaGetLastError();
+    }
+    k_dwconv_ln<<<cdiv(npix, 8), 256, 0, st>>>(x, B, H, W, C, w9, bias, g, b, eps, out);
     return cudaGetLastError();
 }
 
