@@ -658,6 +658,59 @@ __global__ void k_query_init(const float* __restrict__ bbox_all, const int32_t* 
     }
 }
 
+// The same for Dm = 256, warp per query: the 64 frequencies 10000^(-2k/128) computed once per CTA
+// (the expression above), lane per 8 consecutive (sin, cos) pairs (two 16-byte stores), 16-byte
+// copies of the query features.  Same values as k_query_init.
+__global__ void __launch_bounds__(256) k_query_init256(const float* __restrict__ bbox_all,
+                                                       const int32_t* __restrict__ idx,
+                                                       const float* __restrict__ lrn,
+                                                       const float* __restrict__ feat, int N, int NQ, int rows,
+                                                       float* __restrict__ refp, __half* __restrict__ sine,
+                                                       float* __restrict__ tgt, __half* __restrict__ tgt16) {
+    constexpr int Dm = 256, half = Dm / 2;
+    __shared__ float inv[half / 2];
+    if (threadIdx.x < half / 2)
+        inv[threadIdx.x] = expf(-logf(10000.0f) * (float)(2 * threadIdx.x) / (float)half);
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int bq = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (bq >= rows) return;
+    const int b = bq / NQ, q = bq - b * NQ;
+    const int t = idx[bq];
+    const float* box = bbox_all + ((size_t)b * N + t) * 4;
+    const float* l = lrn + (size_t)q * 4;
+    float rp[4];
+    rp[0] = l[0] * box[2] + box[0];
+    rp[1] = l[1] * box[3] + box[1];
+    rp[2] = expf(l[2]) * box[2];
+    rp[3] = expf(l[3]) * box[3];
+    if (lane < 4) refp[(size_t)bq * 4 + lane] = rp[lane];
+    // pairs 8 lane .. 8 lane + 7: component c = lane / 8 (64 pairs each), in [y, x, w, h] order
+    const int comp[4] = {1, 0, 2, 3};
+    const int c = lane >> 3, kp0 = (lane & 7) * 8;
+    const float v = rp[comp[c]] * 6.28318530717958647692f;
+    uint32_t h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float arg = v * inv[kp0 + i];
+        const __half2 sc = __floats2half2_rn(sinf(arg), cosf(arg));
+        h[i] = *reinterpret_cast<const uint32_t*>(&sc);
+    }
+    uint4* so = reinterpret_cast<uint4*>(sine + (size_t)bq * 2 * Dm + c * half + 2 * kp0);
+    so[0] = make_uint4(h[0], h[1], h[2], h[3]);
+    so[1] = make_uint4(h[4], h[5], h[6], h[7]);
+    const float4* f = reinterpret_cast<const float4*>(feat + (size_t)q * Dm) + 2 * lane;
+    const float4 f0 = f[0], f1 = f[1];
+    float4* to = reinterpret_cast<float4*>(tgt + (size_t)bq * Dm) + 2 * lane;
+    to[0] = f0;
+    to[1] = f1;
+    const __half2 a0 = __floats2half2_rn(f0.x, f0.y), a1 = __floats2half2_rn(f0.z, f0.w);
+    const __half2 a2 = __floats2half2_rn(f1.x, f1.y), a3 = __floats2half2_rn(f1.z, f1.w);
+    reinterpret_cast<uint4*>(tgt16 + (size_t)bq * Dm)[lane] =
+        make_uint4(*reinterpret_cast<const uint32_t*>(&a0), *reinterpret_cast<const uint32_t*>(&a1),
+                   *reinterpret_cast<const uint32_t*>(&a2), *reinterpret_cast<const uint32_t*>(&a3));
+}
+
 __global__ void k_add_to_f16(const float* __restrict__ a, const float* __restrict__ b, size_t n,
                              __half* __restrict__ out) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -1186,6 +1239,13 @@ cudaError_t topk_tokens(const float* cls, int B, int N, int NC, int K, int32_t* 
 
 cudaError_t query_init(const float* bbox_all, const int32_t* idx, const float* lrn_rp, const float* feat, int B,
                        int N, int NQ, int Dm, float* refp, __half* sine, float* tgt, __half* tgt16, cudaStream_t st) {
+    auto al = [](const void* q) { return !((uintptr_t)q & 15); };
+    if (Dm == 256 && al(feat) && al(sine) && al(tgt) && al(tgt16)) {
+        const int rows = B * NQ;
+        if (rows > 0) k_query_init256<<<cdiv((size_t)rows, 8), 256, 0, st>>>(bbox_all, idx, lrn_rp, feat, N, NQ, rows,
+                                                                          refp, sine, tgt, tgt16);
+        return cudaGetLastError();
+    }
     k_query_init<<<B * NQ, 256, 0, st>>>(bbox_all, idx, lrn_rp, feat, N, NQ, Dm, refp, sine, tgt, tgt16);
     return cudaGetLastError();
 }
