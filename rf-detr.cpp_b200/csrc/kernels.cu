@@ -101,6 +101,61 @@ __global__ void k_patch_im2col(const float* __restrict__ img, int B, int S, int 
 // elements past 3 p^2 are the zero K padding.  Without resizing, every element
 // is (u / 255 - mean_c) / std_c of a source byte u: a per-block table of those
 // 768 floats (the same float expression) replaces the two divisions.
+// Identity-size patch extraction, CTA per (image, patch row): the patch row's p image rows are
+// one contiguous block of p * S * 3 bytes, loaded with 16-byte loads into shared memory; the CTA
+// then writes the G patches of that row (A rows in window order) as 16-byte chunks of 8 f16, each
+// value lut[c][byte] through the same table as k_patch_from_rgb (identical values).
+// smem: table [3][256] f32, per-k source offset (byte offset within a patch | channel << 24),
+// the strip.
+__global__ void __launch_bounds__(256) k_patch_strip(const uint8_t* __restrict__ rgb, int S, int p, int nw, int Kpad,
+                                                     float m0, float m1, float m2, float s0, float s1, float s2,
+                                                     __half* __restrict__ A) {
+    extern __shared__ uint4 strip_smem[];
+    float* lut = reinterpret_cast<float*>(strip_smem);
+    int* koff = reinterpret_cast<int*>(lut + 3 * 256);
+    uint8_t* strip = reinterpret_cast<uint8_t*>(koff + ((Kpad + 3) & ~3));
+    const int G = S / p, gy = blockIdx.x, b = blockIdx.y;
+    const int row_bytes = S * 3, strip_bytes = p * row_bytes;
+    const uint4* src = reinterpret_cast<const uint4*>(rgb + ((size_t)b * S + (size_t)gy * p) * row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(strip);
+    for (int i = threadIdx.x; i < strip_bytes / 16; i += blockDim.x) dst[i] = __ldg(src + i);
+    for (int t = threadIdx.x; t < 3 * 256; t += blockDim.x) {
+        const int cc = t >> 8;
+        const float mean = cc == 0 ? m0 : (cc == 1 ? m1 : m2), sd = cc == 0 ? s0 : (cc == 1 ? s1 : s2);
+        lut[t] = ((float)(t & 255) / 255.0f - mean) / sd;
+    }
+    const int pp = p * p, kreal = 3 * pp;
+    for (int k = threadIdx.x; k < Kpad; k += blockDim.x) {
+        if (k < kreal) {
+            const int c = k / pp, ky = (k - c * pp) / p, kx = k - c * pp - ky * p;
+            koff[k] = (ky * row_bytes + kx * 3 + c) | (c << 24);
+        } else {
+            koff[k] = -1;
+        }
+    }
+    __syncthreads();
+    const int ws = G / nw, Tp = ws * ws, NT = nw * nw * Tp;
+    const int wy = gy / ws, ty = gy - wy * ws;
+    const int chunks = Kpad / 8;
+    // consecutive threads take consecutive patches of one chunk: the offset-table reads are broadcasts
+    for (int i = threadIdx.x; i < G * chunks; i += blockDim.x) {
+        const int ch = i / G, gx = i - ch * G;
+        const int wx = gx / ws, tx = gx - wx * ws;
+        const size_t row = (size_t)b * NT + (size_t)(wy * nw + wx) * Tp + ty * ws + tx;
+        const uint8_t* patch = strip + gx * p * 3;
+        uint32_t out[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            const int o0 = koff[ch * 8 + e], o1 = koff[ch * 8 + e + 1];
+            const float v0 = o0 < 0 ? 0.f : lut[((o0 >> 24) << 8) + patch[o0 & 0xFFFFFF]];
+            const float v1 = o1 < 0 ? 0.f : lut[((o1 >> 24) << 8) + patch[o1 & 0xFFFFFF]];
+            const __half2 hv = __floats2half2_rn(v0, v1);
+            out[e >> 1] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        reinterpret_cast<uint4*>(A + row * Kpad)[ch] = make_uint4(out[0], out[1], out[2], out[3]);
+    }
+}
+
 __global__ void __launch_bounds__(256) k_patch_from_rgb(const uint8_t* __restrict__ rgb, int B, int w, int h, int S,
                                                         int p, int nw, int Kpad, float m0, float m1, float m2,
                                                         float s0, float s1, float s2, __half* __restrict__ A) {
@@ -1053,6 +1108,14 @@ cudaError_t patch_from_rgb(const uint8_t* rgb, int B, int w, int h, int S, int p
     const size_t rows = (size_t)B * nw * nw * Tp;
     if (Kpad % 8 || Kpad < 3 * p * p || ((uintptr_t)A & 15)) return cudaErrorInvalidValue;  // 16-byte stores
     if (rows >= (1u << 21)) return cudaErrorInvalidValue;
+    // identity size with 16-byte aligned strips: CTA per (image, patch row)
+    const size_t strip_smem = 3 * 256 * 4 + (size_t)((Kpad + 3) & ~3) * 4 + (size_t)p * S * 3;
+    if (w == S && h == S && S % p == 0 && ((size_t)p * S * 3) % 16 == 0 && !((uintptr_t)rgb & 15) &&
+        strip_smem <= 48 * 1024 && B <= 65535) {
+        k_patch_strip<<<dim3(S / p, B), 256, strip_smem, st>>>(rgb, S, p, nw, Kpad, mean3[0], mean3[1], mean3[2],
+                                                               std3[0], std3[1], std3[2], A);
+        return cudaGetLastError();
+    }
     const unsigned blocks = cdiv(rows, 8) < 148u * 8u ? cdiv(rows, 8) : 148u * 8u;  // warp per row, grid-strided
     k_patch_from_rgb<<<blocks, 256, 0, st>>>(rgb, B, w, h, S, p, nw, Kpad, mean3[0], mean3[1], mean3[2],
                                                    std3[0], std3[1], std3[2], A);
