@@ -165,6 +165,44 @@ def backbone_gemm_flops(cfg, batch):
     return {"qkv": 2 * M * D * 3 * D, "proj": 2 * M * D * D, "fc1": 2 * M * D * F, "fc2": 2 * M * F * D}
 
 
+def backbone_gemm_bytes(cfg, batch):
+    """Algorithmic HBM bytes of the same launches: each f16 operand read once, each output
+    written once; the residual linears (proj, fc2) read and write the f32 residual stream."""
+    S, p, nw = cfg["image_size"], cfg["patch_size"], cfg["backbone"]["num_windows"]
+    G = S // p
+    ws = G // nw
+    ntok = nw * nw * (ws * ws + 1)
+    D, F = cfg["backbone"]["dim"], cfg["backbone"]["ffn_dim"]
+    M = batch * ntok
+    return {"qkv": 2 * (M * D + 3 * D * D + M * 3 * D),
+            "proj": 2 * (M * D + D * D) + 8 * M * D,
+            "fc1": 2 * (M * D + F * D + M * F),
+            "fc2": 2 * (M * F + D * F) + 8 * M * D}
+
+
+def gemm_parts(fl, by, g_ms, g_n, hbm_gbs, tf_peak):
+    """Per-linear figures of one profiled forward: time, TFLOP/s and GB/s against the
+    tensor and HBM peaks, and which of the two bounds the launch (the larger of
+    FLOPs / tensor peak and bytes / HBM peak).  `own_bound_frac` is the sum over launches
+    of that bound's time divided by their measured time."""
+    parts, t_bound, t_meas = {}, 0.0, 0.0
+    for k in fl:
+        n, ms = g_n.get(k, 0), g_ms.get(k, 0.0)
+        if n == 0 or ms <= 0:
+            continue
+        t_t = fl[k] * n / (tf_peak * 1e12) * 1e3
+        t_h = by[k] * n / (hbm_gbs * 1e9) * 1e3
+        parts[k] = {"launches": n, "ms": round(ms, 4),
+                    "tflops": round(fl[k] * n / (ms / 1e3) / 1e12, 1),
+                    "frac_tensor": round(t_t / ms, 4),
+                    "gbs": round(by[k] * n / (ms / 1e3) / 1e9, 1),
+                    "frac_hbm": round(t_h / ms, 4),
+                    "bound": "tensor" if t_t >= t_h else "hbm"}
+        t_bound += max(t_t, t_h)
+        t_meas += ms
+    return parts, (round(t_bound / t_meas, 4) if t_meas > 0 else None)
+
+
 def peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
@@ -451,6 +489,7 @@ def main():
     total_ms = sum(t for _, t in prof)
     hbm, tf_burst, tf_sus, src = peaks()
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
+    parts, own_frac = gemm_parts(fl, backbone_gemm_bytes(cfg, B), g_ms, g_n, hbm, tf_sus)
     tr = traffic_from_profiles()
     share = {}
     for name, t_ms in prof:
@@ -517,7 +556,9 @@ def main():
                          "timing": "per-launch CUDA events of one forward launched kernel by kernel outside "
                                    "the CUDA graph the timed steps replay (conservative)",
                          "gemm_ms": round(gemm_ms, 4), "forward_ms": round(total_ms, 4),
-                         "gemm_share": round(gemm_ms / total_ms, 4) if total_ms else None},
+                         "gemm_share": round(gemm_ms / total_ms, 4) if total_ms else None,
+                         "parts": parts,
+                         "own_bound_frac": own_frac},
             "top_launches_ms": [[k, round(v, 4)] for k, v in top],
             "clocks": clk,
         }

@@ -1,6 +1,6 @@
 """Micro-benchmark of single engine operators at model shapes.
 
-    python bench_kernels.py gemm --m 51712 --n 1536 --k 384 [--epi 0 --act 1]
+    python bench_kernels.py gemm --m 51712 --n 1536 --k 384 [--epi 0 --act 1] [--cublas]
     python bench_kernels.py attn --seq 1616 --groups 32 --heads 6 --hd 64
     python bench_kernels.py deform --batch 32 --grid 40 --nq 300 --heads 16 --points 2
     python bench_kernels.py topk --batch 1 --grid 40 --nc 91 --nq 300
@@ -12,7 +12,9 @@ for attention) or GB/s for the deformable sampling (algorithmic bytes: the
 value map read once, the offset/logit rows, the reference points and the f16
 output) and the two-stage top-K (the grid x grid x nc f32 class logits of each
 image read once, the nq int32 indices written).  Used for ncu captures of one
-kernel in isolation.
+kernel in isolation.  `gemm --cublas` times the library GEMM of the same shape
+instead (torch.matmul, f16 in and out, no bias or activation) as a point of
+comparison; it is not part of the engine.
 """
 import argparse
 import json
@@ -46,6 +48,7 @@ def main():
     ap.add_argument("--nc", type=int, default=91)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--cublas", action="store_true")
     a = ap.parse_args()
     L = lib.lib()
     dev = "cuda:0"
@@ -66,6 +69,12 @@ def main():
             assert rc == 0, rc
         flops = 2.0 * a.m * a.n * a.k
         name = f"gemm M={a.m} N={a.n} K={a.k} epi={a.epi} act={a.act}"
+        if a.cublas:
+            Bt = B.t()
+
+            def run():
+                torch.matmul(A, Bt, out=out16)
+            name = f"cublas gemm M={a.m} N={a.n} K={a.k} (f16 out, no epilogue)"
     elif a.op == "deform":
         H, P, Dm, NQ, G, B = a.heads, a.points, a.dm, a.nq, a.grid, a.batch
         ld = H * P * 3

@@ -21,6 +21,28 @@ def test_backbone_gemm_flops_of_base():
     assert bench.backbone_gemm_flops(cfg, 32)["qkv"] == 32 * per["qkv"]
 
 
+def test_backbone_gemm_bytes_and_bounds_of_base():
+    """Base batch 64 (M = 103424 rows): qkv and fc1 are bound by the tensor peak, proj by
+    HBM (its f32 residual read-modify-write), and the per-launch fractions recombine."""
+    import bench
+    from rfdetr_b200 import synth
+
+    cfg = synth.get_variant("base")
+    by = bench.backbone_gemm_bytes(cfg, 64)
+    M, D, F = 103424, 384, 1536
+    assert by["proj"] == 2 * (M * D + D * D) + 8 * M * D
+    assert by["fc2"] == 2 * (M * F + D * F) + 8 * M * D
+    fl = bench.backbone_gemm_flops(cfg, 64)
+    g_ms = {"qkv": 0.105, "proj": 0.0736, "fc1": 0.155, "fc2": 0.135}
+    g_n = {k: 1 for k in g_ms}
+    parts, own = bench.gemm_parts(fl, by, g_ms, g_n, 6545.0, 1368.8)
+    assert parts["qkv"]["bound"] == "tensor" and parts["fc1"]["bound"] == "tensor"
+    assert parts["proj"]["bound"] == "hbm" and parts["fc2"]["bound"] == "hbm"
+    t_bound = sum(max(parts[k]["frac_tensor"], parts[k]["frac_hbm"]) * g_ms[k] for k in g_ms)
+    assert abs(own - t_bound / sum(g_ms.values())) < 1e-3
+    assert 0.5 < parts["proj"]["frac_hbm"] < 1.0
+
+
 def _clocks(rows):
     import bench
 
