@@ -133,3 +133,45 @@ def test_mask_bits_match_oracle_upsample(w, h):
     # a detection count beyond max_dets is rejected before any launch
     assert _lib().rfdetr_b200_op_mask_bits(_p(dm), B, NQ, side, _p(d_dets), _p(d_cnt), NQ + 1, w, h, _p(bits),
                                            _stream()) != 0
+
+
+def test_select_and_masks_match_the_reference_code():
+    """Device selection and mask bits on the seeded cases of tests/golden/host_ref.npz, which hold
+    the outputs of the reference's own src/postprocess.cpp (built from the reference tree): the
+    same records in the same order, except that runs of equal score (the reference sorts them with
+    std::sort) are compared as sets; scores to 1e-6 relative (the device's exp), boxes to 1e-3 px,
+    masks (square mask cases) pixel for pixel."""
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import gen_host_ref_golden as gen
+
+    g = np.load(os.path.join(ROOT, "tests", "golden", "host_ref.npz"))
+    for seed, nq, nc, thr, top_k, flt, iw, ih, mw, mh, sat in gen.SEL_CASES:
+        lg, bx, mk = gen.sel_inputs(seed, nq, nc, mw, mh, sat)
+        got, d_dets, d_cnt = _select(lg[None], bx[None], thr, top_k, iw, ih, list(flt) if flt else None)
+        q, c, s, xy = got[0]
+        rc_, rs = g[f"sel_{seed}_class"], g[f"sel_{seed}_score"].view(np.float32)
+        rxy = g[f"sel_{seed}_box"].view(np.float32)
+        assert len(q) == len(rc_), f"case {seed}: {len(q)} records, reference {len(rc_)}"
+        masks_ok = mw and mw == mh
+        if masks_ok:
+            words = _lib().rfdetr_b200_mask_bits_words(iw, ih)
+            bits = torch.zeros(max(1, len(q)) * words, dtype=torch.int32, device="cuda")
+            dm = torch.from_numpy(mk[None]).cuda()
+            assert _lib().rfdetr_b200_op_mask_bits(_p(dm), 1, nq, mw, _p(d_dets), _p(d_cnt), max(1, len(q)), iw,
+                                                   ih, _p(bits), _stream()) == 0
+            torch.cuda.synchronize()
+            u = bits.cpu().numpy().view(np.uint32).reshape(max(1, len(q)), ih, -1)
+            px = np.arange(iw)
+            ours = [((u[i][:, px // 32] >> (px % 32).astype(np.uint32)) & 1).astype(np.uint8) * 255
+                    for i in range(len(q))]
+            rmk = g[f"sel_{seed}_mask"]
+        for a, e in gen.tie_runs(g[f"sel_{seed}_score"].tolist()):
+            key = lambda cls, box: (int(cls),) + tuple(np.round(box, 2))  # noqa: E731
+            mine = sorted(range(a, e), key=lambda i: key(c[i], xy[i]))
+            refs = sorted(range(a, e), key=lambda i: key(rc_[i], rxy[i]))
+            for i, j in zip(mine, refs):
+                assert c[i] == rc_[j], f"case {seed} record {i}"
+                assert np.isclose(s[i], rs[j], rtol=1e-6, atol=0), f"case {seed} record {i}"
+                assert np.allclose(xy[i], rxy[j], atol=1e-3), f"case {seed} record {i}"
+                if masks_ok:
+                    assert (ours[i] == rmk[j]).mean() >= 0.99999, f"case {seed} mask of record {i}"
