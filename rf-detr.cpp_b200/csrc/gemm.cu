@@ -239,7 +239,9 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         uint8_t* wptr = out_stage + quad * 8192 + half * 4096;
         const uint32_t wbuf = smem_u32(wptr);
         constexpr bool kSplit = (EPI == EPI_LN) || (BN >= 128);
-        constexpr int kHalf0 = ((BN / 2 + 63) / 64) * 64;  // first half: whole 64-column chunks
+        // first half: whole chunks (64 columns for f16 outputs, 32 for the f32 and patch paths)
+        constexpr int kChunk = EPI == EPI_F16 ? 64 : 32;
+        constexpr int kHalf0 = ((BN / 2 + kChunk - 1) / kChunk) * kChunk;
         const bool active = kSplit || half == 0;
         const int col_begin = kSplit ? half * kHalf0 : 0;
         const int col_end = kSplit ? (half ? BN : kHalf0) : BN;
@@ -513,7 +515,21 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
             } else if (EPI == EPI_PATCH && p.patch_vec) {
                 // window remap + position add: each 32-column chunk goes through the warp's staging box,
                 // then 8 lanes write one 128-byte row (4 rows per instruction), so the remapped stores
-                // and the position loads are coalesced
+                // and the position loads are coalesced.  A lane's eight rows are the same for every
+                // chunk of the tile: their output and position rows are found once per tile, and
+                // all eight position loads of a chunk are issued before the stores.
+                long long orow[8];
+                int prow[8];
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    const int mr = mt * BM + quad * 32 + it * 4 + (lane >> 3);
+                    const int img = mr / p.patch_rows;
+                    const int rr = mr - img * p.patch_rows;
+                    const int win = rr / p.patch_tp;
+                    const int tok = win * p.patch_t + 1 + (rr - win * p.patch_tp);
+                    orow[it] = mr < p.M ? ((long long)img * p.patch_ntok + tok) * p.ld32 : -1;
+                    prow[it] = tok * p.N;
+                }
                 for (int c0 = col_begin; c0 < col_end; c0 += 32) {
                     tmem_ld32(tbase + c0, raw);
                     const int n0 = nt * BN + c0;
@@ -530,19 +546,18 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     __syncwarp();
                     const int ch = lane & 7;
                     const int n = n0 + 4 * ch;
-#pragma unroll 2
-                    for (int it = 0; it < 8; ++it) {
-                        const int r = it * 4 + (lane >> 3);
-                        const int mr = mt * BM + quad * 32 + r;
-                        if (mr < p.M && n < p.N) {
-                            float4 x = ld_shared_v4f(swz(wbuf, r, ch));
-                            const int img = mr / p.patch_rows;
-                            const int rr = mr - img * p.patch_rows;
-                            const int win = rr / p.patch_tp;
-                            const int tok = win * p.patch_t + 1 + (rr - win * p.patch_tp);
-                            const float4 ps = __ldg(reinterpret_cast<const float4*>(p.posw + (size_t)tok * p.N + n));
-                            x.x += ps.x; x.y += ps.y; x.z += ps.z; x.w += ps.w;
-                            *reinterpret_cast<float4*>(p.out32 + ((size_t)img * p.patch_ntok + tok) * p.ld32 + n) = x;
+                    if (n < p.N) {
+                        float4 ps[8];
+#pragma unroll
+                        for (int it = 0; it < 8; ++it)
+                            ps[it] = orow[it] >= 0 ? __ldg(reinterpret_cast<const float4*>(p.posw + prow[it] + n))
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int it = 0; it < 8; ++it) {
+                            if (orow[it] < 0) continue;
+                            float4 x = ld_shared_v4f(swz(wbuf, it * 4 + (lane >> 3), ch));
+                            x.x += ps[it].x; x.y += ps[it].y; x.z += ps[it].z; x.w += ps[it].w;
+                            *reinterpret_cast<float4*>(p.out32 + orow[it] + n) = x;
                         }
                     }
                     __syncwarp();
@@ -562,11 +577,31 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
 #pragma unroll
                         for (int j = 0; j < 32; ++j) v[j] *= bcast(sl, j);
                     }
+                    if constexpr (EPI == EPI_F32) {
+                        // through the warp's staging box: each store instruction then writes 32
+                        // consecutive columns of one row instead of one value of 32 rows.  The
+                        // quadrant's rows are consecutive (m - lane + r), the ballot marks the
+                        // valid ones.
+                        const unsigned okmask = __ballot_sync(0xffffffffu, row_ok);
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            st_shared_v4(swz(wbuf, lane, j), __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                                         __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+                        __syncwarp();
+                        if (nok) {
+                            float* col = p.out32 + boff + (long long)(m - lane) * p.ld32 + n0 + lane;
+#pragma unroll 8
+                            for (int r = 0; r < 32; ++r)
+                                if ((okmask >> r) & 1u)
+                                    col[(long long)r * p.ld32] = ld_shared_f32(swz(wbuf, r, lane >> 2) + (lane & 3) * 4);
+                        }
+                        __syncwarp();
+                        continue;
+                    }
                     if (!row_ok || n0 >= p.N) continue;
                     if constexpr (EPI == EPI_F16) {
                         store_row_f16(p.out16 + boff + (size_t)m * p.ld16 + n0, v, n0, p.N);
-                    } else if constexpr (EPI == EPI_F32) {
-                        store_row_f32(p.out32 + boff + (size_t)m * p.ld32 + n0, v, n0, p.N);
                     } else if constexpr (EPI == EPI_RESID) {
                         float* dst = p.out32 + boff + (size_t)m * p.ld32 + n0;
 #pragma unroll
