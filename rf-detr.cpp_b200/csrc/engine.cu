@@ -656,9 +656,15 @@ rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int 
 
     // ---- backbone blocks (src/dinov2.cpp:432-538)
     const float scale = 1.0f / std::sqrt((float)(D / H_));
+    // a tapped block's output is normalised once for its tap and the next block's norm1
+    // (RFDETR_LN_TAP=0: two launches; the outputs are the same bit for bit)
+    const char* ln_tap_env = std::getenv("RFDETR_LN_TAP");
+    const bool fuse_tap = !(ln_tap_env && ln_tap_env[0] == '0');
+    bool ln1_done = false;
     for (size_t i = 0; i < blocks_.size(); ++i) {
         const Block& bk = blocks_[i];
-        L.check(layernorm(x_, Mb, D, bk.ln1.g, bk.ln1.b, 1e-6f, nullptr, h16_, st), "ln1");
+        if (!ln1_done) L.check(layernorm(x_, Mb, D, bk.ln1.g, bk.ln1.b, 1e-6f, nullptr, h16_, st), "ln1");
+        ln1_done = false;
         L.gemm("qkv", h16_, D, Mb, bk.qkv, EPI_F16, ACT_NONE, nullptr, 0, qkv_, 3 * D);
         if (bk.global)
             L.check(attention_tc(qkv_, qkv_ + D, qkv_ + 2 * D, 3 * D, 3 * D, 3 * D, attn_, D, Ntok_, B, H_, scale, d_err_,
@@ -672,8 +678,15 @@ rfdetr_status Engine::enqueue_raw(int B, const uint8_t* src_rgb, int src_w, int 
         L.check(layernorm(x_, Mb, D, bk.ln2.g, bk.ln2.b, 1e-6f, nullptr, h16_, st), "ln2");
         L.gemm("fc1", h16_, D, Mb, bk.fc1, EPI_F16, ACT_GELU, nullptr, 0, f1_, F_);
         L.gemm("fc2", f1_, F_, Mb, bk.fc2, EPI_RESID, ACT_NONE, x_, D, nullptr, 0, bk.ls2);
-        if (bk.tap >= 0)
+        if (bk.tap >= 0 && fuse_tap && i + 1 < blocks_.size()) {
+            const Block& nb = blocks_[i + 1];
+            L.check(layernorm_and_tap(x_, B, G, nw_, D, nb.ln1.g, nb.ln1.b, h16_, bbnorm_.g, bbnorm_.b, taps_, L_ * D,
+                                      bk.tap * D, st),
+                    "ln1+tap");
+            ln1_done = true;
+        } else if (bk.tap >= 0) {
             L.check(backbone_tap(x_, B, G, nw_, D, bbnorm_.g, bbnorm_.b, taps_, L_ * D, bk.tap * D, st), "tap");
+        }
     }
 
     // ---- projector (src/projector.cpp:85-189), token-major

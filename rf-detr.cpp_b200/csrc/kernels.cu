@@ -368,6 +368,100 @@ __global__ void __launch_bounds__(256) k_layernorm_v4(const float* x, int rows, 
     }
 }
 
+// A tapped block's output read once for two LayerNorms with the same statistics (eps 1e-6 both):
+// the next block's norm1 (src/dinov2.cpp:17-23, y16 row r = x row r, window order) and the
+// backbone tap (src/dinov2.cpp:490-537: the final norm, CLS rows dropped, written at grid pixel
+// (b, gy, gx), column col0 of an f16 row of pitch ld).  The arithmetic is k_layernorm_v4's, so
+// both outputs equal those of the two separate launches bit for bit.
+struct DualTapMap {
+    int G = 0, nw = 1, ld = 0, col0 = 0;
+    float inv_bt = 0.f, inv_t = 0.f, inv_ws = 0.f, inv_nw = 0.f;  // 1 / (nw^2 T), 1 / T, 1 / ws, 1 / nw
+    // grid row of window-order token row r, or -1 for a CLS row
+    __device__ __forceinline__ long long dst_row(int r) const {
+        const int ws = G / nw, T = ws * ws + 1, BT = nw * nw * T;
+        const int b = div_small(r, inv_bt), rr = r - b * BT;
+        const int win = div_small(rr, inv_t), t = rr - win * T;
+        if (t == 0) return -1;
+        const int py = div_small(t - 1, inv_ws), px = (t - 1) - py * ws;
+        const int wy = div_small(win, inv_nw), wx = win - wy * nw;
+        return ((long long)b * G + wy * ws + py) * G + wx * ws + px;
+    }
+};
+
+template <int NV>
+__global__ void __launch_bounds__(256) k_layernorm_dual(const float* x, int rows, const float* __restrict__ g1,
+                                                       const float* __restrict__ b1, __half* __restrict__ y16,
+                                                       const float* __restrict__ g2, const float* __restrict__ b2,
+                                                       __half* __restrict__ taps, DualTapMap tm) {
+    constexpr int D = 128 * NV;
+    constexpr float eps = 1e-6f;
+    const int lane = threadIdx.x & 31;
+    const int stride = gridDim.x * (blockDim.x >> 5);
+    int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    float4 ga[NV], ba[NV], gt[NV], bt[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        ga[i] = *reinterpret_cast<const float4*>(g1 + 4 * (lane + 32 * i));
+        ba[i] = *reinterpret_cast<const float4*>(b1 + 4 * (lane + 32 * i));
+        gt[i] = *reinterpret_cast<const float4*>(g2 + 4 * (lane + 32 * i));
+        bt[i] = *reinterpret_cast<const float4*>(b2 + 4 * (lane + 32 * i));
+    }
+    float4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = reinterpret_cast<const float4*>(x + (size_t)row * D)[lane + 32 * i];
+    for (; row < rows; row += stride) {
+        const int nxt = row + stride;
+        float4 vn[NV];
+        if (nxt < rows) {
+            const float4* xn = reinterpret_cast<const float4*>(x + (size_t)nxt * D);
+#pragma unroll
+            for (int i = 0; i < NV; ++i) vn[i] = xn[lane + 32 * i];
+        }
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        const float mean = warp_sum(s) / (float)D;
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const float a = v[i].x - mean, bq = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+            q += (a * a + bq * bq) + (c * c + d * d);
+        }
+        const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)D + eps);
+        const long long trow = tm.dst_row(row);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c0 = 4 * (lane + 32 * i);
+            float4 o;
+            o.x = (v[i].x - mean) * rstd * ga[i].x + ba[i].x;
+            o.y = (v[i].y - mean) * rstd * ga[i].y + ba[i].y;
+            o.z = (v[i].z - mean) * rstd * ga[i].z + ba[i].z;
+            o.w = (v[i].w - mean) * rstd * ga[i].w + ba[i].w;
+            __half2 h0 = __floats2half2_rn(o.x, o.y), h1 = __floats2half2_rn(o.z, o.w);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t*>(&h0);
+            u.y = *reinterpret_cast<uint32_t*>(&h1);
+            *reinterpret_cast<uint2*>(y16 + (size_t)row * D + c0) = u;
+            if (trow >= 0) {
+                o.x = (v[i].x - mean) * rstd * gt[i].x + bt[i].x;
+                o.y = (v[i].y - mean) * rstd * gt[i].y + bt[i].y;
+                o.z = (v[i].z - mean) * rstd * gt[i].z + bt[i].z;
+                o.w = (v[i].w - mean) * rstd * gt[i].w + bt[i].w;
+                h0 = __floats2half2_rn(o.x, o.y);
+                h1 = __floats2half2_rn(o.z, o.w);
+                u.x = *reinterpret_cast<uint32_t*>(&h0);
+                u.y = *reinterpret_cast<uint32_t*>(&h1);
+                *reinterpret_cast<uint2*>(taps + trow * tm.ld + tm.col0 + c0) = u;
+            }
+        }
+        if (nxt < rows) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) v[i] = vn[i];
+        }
+    }
+}
+
 // ---- backbone tap: src/dinov2.cpp:490-537 -----------------------------------
 __global__ void k_tap(const float* __restrict__ x, int B, int G, int nw, int D, const float* __restrict__ g,
                       const float* __restrict__ bb, __half* __restrict__ taps, int ld, int col0) {
@@ -1256,6 +1350,31 @@ cudaError_t backbone_tap(const float* x, int B, int G, int nw, int D, const floa
         return cudaGetLastError();
     }
     k_tap<<<cdiv((size_t)rows, 8), 256, 0, st>>>(x, B, G, nw, D, g, b, taps, ld, col0);
+    return cudaGetLastError();
+}
+
+cudaError_t layernorm_and_tap(const float* x, int B, int G, int nw, int D, const float* g1, const float* b1,
+                              __half* y16, const float* g2, const float* b2, __half* taps, int ld, int col0,
+                              cudaStream_t st) {
+    const int ws = G / nw, T = ws * ws + 1;
+    const long long rows = (long long)B * nw * nw * T;
+    const bool fused = (D == 384 || D == 256) && rows < (1 << 21) && ld % 4 == 0 && col0 % 4 == 0 &&
+                       !(((uintptr_t)x | (uintptr_t)y16 | (uintptr_t)taps) & 15) &&
+                       !(((uintptr_t)g1 | (uintptr_t)b1 | (uintptr_t)g2 | (uintptr_t)b2) & 15);
+    if (!fused) {
+        const cudaError_t e = layernorm(x, (int)rows, D, g1, b1, 1e-6f, nullptr, y16, st);
+        if (e != cudaSuccess) return e;
+        return backbone_tap(x, B, G, nw, D, g2, b2, taps, ld, col0, st);
+    }
+    DualTapMap tm;
+    tm.G = G; tm.nw = nw; tm.ld = ld; tm.col0 = col0;
+    tm.inv_bt = 1.0f / (float)(nw * nw * T);
+    tm.inv_t = 1.0f / (float)T;
+    tm.inv_ws = 1.0f / (float)ws;
+    tm.inv_nw = 1.0f / (float)nw;
+    const unsigned blocks = cdiv((size_t)rows, 8) < (unsigned)(148 * 6) ? cdiv((size_t)rows, 8) : (unsigned)(148 * 6);
+    if (D == 384) k_layernorm_dual<3><<<blocks, 256, 0, st>>>(x, (int)rows, g1, b1, y16, g2, b2, taps, tm);
+    else k_layernorm_dual<2><<<blocks, 256, 0, st>>>(x, (int)rows, g1, b1, y16, g2, b2, taps, tm);
     return cudaGetLastError();
 }
 

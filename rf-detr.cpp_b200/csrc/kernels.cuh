@@ -36,6 +36,14 @@ cudaError_t resize_legacy_rgb(const uint8_t* src, int B, int w, int h, const Leg
 cudaError_t patch_from_rgb(const uint8_t* rgb, int B, int w, int h, int S, int p, int nw, int Kpad,
                            const float* mean3, const float* std3, __half* A, cudaStream_t st);
 
+// The output x of a tapped backbone block (window order, B * nw^2 * T rows of D f32) normalised
+// twice with the same row statistics (eps 1e-6): y16 = LayerNorm(x; g1, b1) row for row (the next
+// block's norm1) and the backbone tap of backbone_tap (g2, b2, CLS rows dropped, grid order, column
+// col0 of f16 rows of pitch ld) from one read of x.
+cudaError_t layernorm_and_tap(const float* x, int B, int G, int nw, int D, const float* g1, const float* b1,
+                              __half* y16, const float* g2, const float* b2, __half* taps, int ld, int col0,
+                              cudaStream_t st);
+
 // x[b][w*T] = clsrow (one CLS token per window).
 cudaError_t write_cls_rows(float* x, const float* clsrow, int B, int NW, int T, int D, cudaStream_t st);
 

@@ -206,6 +206,27 @@ def test_graph_replay_matches_direct_launches(make_model, monkeypatch):
     assert np.array_equal(lb_direct, lb_direct2)
 
 
+@pytest.mark.parametrize("variant,dtype,S", [("tiny", "f16", 128), ("base", "q8_0", 560)])
+def test_fused_norm1_and_tap_match_separate_launches(variant, dtype, S, make_model, monkeypatch):
+    """A tapped block's output is normalised once for the backbone tap and the next block's norm1
+    (one launch reading x once); the forward must equal, bit for bit, the one with the two
+    separate LayerNorm launches (RFDETR_LN_TAP=0), including the projector input the taps feed."""
+    from rfdetr_b200 import lib
+
+    path = make_model(variant, dtype, 0)
+    imgs = _images(S, 2, 31)
+    outs = []
+    for env in ("1", "0"):
+        monkeypatch.setenv("RFDETR_LN_TAP", env)
+        eng = lib.Engine(path, max_batch=2)
+        lg, bx, _ = eng.forward_rgb(imgs)
+        proj = eng.trace("projector.output", 2)
+        eng.close()
+        outs.append((lg, bx, proj))
+    for a, b in zip(outs[0], outs[1]):
+        assert np.array_equal(a, b)
+
+
 def test_split_k_layernorm_gemms_match_the_oracle(make_model):
     """With few row blocks (batch 1: 300 decoder rows, one 24 x 24 grid) the LayerNorm GEMMs run as
     split-K f32 partial sums plus an in-order row reduction: the forward repeats bit for bit and
