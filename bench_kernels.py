@@ -49,6 +49,8 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--cublas", action="store_true")
+    ap.add_argument("--ln", type=int, default=0, help="gemm: LayerNorm epilogue (epi 4): 1 = plain, 2 = with a "
+                                                         "residual and f32 + f16 outputs (the decoder's form)")
     a = ap.parse_args()
     L = lib.lib()
     dev = "cuda:0"
@@ -59,16 +61,22 @@ def main():
         B = (torch.randn(a.n, a.k, device=dev, generator=g) * 0.05).half()
         bias = torch.zeros(a.n, device=dev)
         out16 = torch.empty(a.m, a.n, dtype=torch.float16, device=dev)
-        out32 = torch.empty(a.m, a.n, device=dev) if a.epi in (1, 2) else None
+        out32 = torch.empty(a.m, a.n, device=dev) if a.epi in (1, 2) or a.ln == 2 else None
+        lng = torch.ones(a.n, device=dev)
+        lnb = torch.zeros(a.n, device=dev)
+        resid = torch.randn(a.m, a.n, device=dev, generator=g) if a.ln == 2 else None
+        epi = 4 if a.ln else a.epi
 
         def run():
-            rc = L.rfdetr_b200_op_gemm(A.data_ptr(), a.k, B.data_ptr(), a.k, a.m, a.n, a.k, a.epi, a.act,
-                                       bias.data_ptr(), None, None, None, 0.0, None, 0,
+            rc = L.rfdetr_b200_op_gemm(A.data_ptr(), a.k, B.data_ptr(), a.k, a.m, a.n, a.k, epi, a.act,
+                                       bias.data_ptr(), None, lng.data_ptr() if a.ln else None,
+                                       lnb.data_ptr() if a.ln else None, 1e-5,
+                                       resid.data_ptr() if resid is not None else None, a.n,
                                        out32.data_ptr() if out32 is not None else None, a.n, out16.data_ptr(),
                                        a.n, st)
             assert rc == 0, rc
         flops = 2.0 * a.m * a.n * a.k
-        name = f"gemm M={a.m} N={a.n} K={a.k} epi={a.epi} act={a.act}"
+        name = f"gemm M={a.m} N={a.n} K={a.k} epi={epi} act={a.act}" + (f" ln={a.ln}" if a.ln else "")
         if a.cublas:
             Bt = B.t()
 
