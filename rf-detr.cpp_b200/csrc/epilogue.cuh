@@ -13,46 +13,26 @@
 namespace rfb {
 namespace {
 
-// erf-GELU, 0.5 v (1 + erf(v / sqrt 2)), written as
-//   GELU(v) = max(v, 0) - a e^{-a^2/2} R(a),  a = min(|v|, 6),
-//   R(a) = 0.5 erfcx(a / sqrt 2)
-// (erfcx = the scaled complementary error function).  -R is a polynomial,
-// a near-minimax fit on [0, 6] weighted by a e^{-a^2/2}: weighted least
-// squares on 200001 points against scipy.special.erfcx, refined by Lawson's
-// iteratively reweighted least squares (C. L. Lawson, 1961), 60 iterations.
-// Evaluated in float32 with exp2, the absolute error of GELU for
-// every input is <= 1.1e-7 with degree 10, <= 7.9e-7 with degree 8 and
-// <= 2.9e-6 with degree 7 (f16 spacing is 9.8e-7 at 0.002 and 2.4e-4 at 0.5);
-// the clamp at 6 adds < 7e-9.  One exp2 and (degree + 1) FMAs per value, no
-// divide: the packed pair form below runs the polynomial on the f32x2 FMA
-// path (two values per instruction).  The epilogue of a GEMM with a GELU is
-// bound by these FMAs, so RFB_GELU_DEGREE trades them against accuracy.
-// Build with -DRFB_GELU_ERFF=1 to use erff instead.
+// erf-GELU, 0.5 v (1 + erf(v / sqrt 2)) = v Phi(v), written as
+//   GELU(v) = max(v, 0) - a 2^L(a),  a = min(|v|, 6),  L(a) = log2 Phi(-a)
+// (v Phi(v) is v - a Phi(-a) for v = a >= 0 and -a Phi(-a) for v = -a; Phi is the
+// standard normal CDF).  L, the Gaussian factor included, is a degree-6 polynomial:
+// a near-minimax fit on [0, 6], weighted so that the error of a 2^L stays below a
+// quarter of the f16 spacing of a Phi(-a) where that is a normal f16 (and 1e-7
+// absolute below), by least squares on 400001 points against scipy.special.log_ndtr
+// refined with Lawson's iteratively reweighted least squares (C. L. Lawson, 1961).
+// Evaluated in float32 with one exp2, |GELU error| <= 3.2e-7 for every input, and
+// 99.93 % of the outputs in the f16 normal range round to the correctly rounded f16;
+// the clamp at 6 adds < 6e-9.  Six FMAs, one exp2 and one FMA per value, no divide:
+// the packed pair form below runs them on the f32x2 FMA path (two values per
+// instruction).  Build with -DRFB_GELU_ERFF=1 to use erff instead.
 #ifndef RFB_GELU_ERFF
 #define RFB_GELU_ERFF 0
 #endif
-#ifndef RFB_GELU_DEGREE
-#define RFB_GELU_DEGREE 8
-#endif
-#if RFB_GELU_DEGREE == 10
-static __constant__ float kGeluNegR[11] = {
-    -9.078557923e-07f, 2.187343125e-05f, -2.361505467e-04f, 1.531139482e-03f, -6.791573483e-03f,
-    2.246006206e-02f, -5.929261073e-02f, 1.313898265e-01f, -2.495388836e-01f, 3.988756537e-01f,
-    -4.999966621e-01f};
-#elif RFB_GELU_DEGREE == 8
-static __constant__ float kGeluNegR[9] = {
-    -2.124682942e-05f, 3.925739147e-04f, -3.196175443e-03f, 1.543588843e-02f, -5.079322681e-02f,
-    1.252110153e-01f, -2.470255792e-01f, 3.983812630e-01f, -4.999636412e-01f};
-#elif RFB_GELU_DEGREE == 7
-static __constant__ float kGeluNegR[8] = {
-    9.495724225e-05f, -1.505025313e-03f, 1.039928570e-02f, -4.231634364e-02f, 1.171148866e-01f,
-    -2.428599894e-01f, 3.973712325e-01f, -4.998818636e-01f};
-#else
-#error "RFB_GELU_DEGREE must be 10, 8 or 7"
-#endif
-constexpr int kGeluTerms = RFB_GELU_DEGREE + 1;
+static __constant__ float kGeluL[7] = {3.525229477e-05f,  -7.827336667e-04f, 8.099309169e-03f, -5.338359997e-02f,
+                                       -4.588511288e-01f, -1.151151538e+00f, -1.000000477e+00f};
+constexpr int kGeluTerms = 7;
 constexpr float kGeluClamp = 6.0f;
-constexpr float kNegHalfLog2e = -0.72134752044448170368f;  // -0.5 / ln 2
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float r;
@@ -65,11 +45,10 @@ __device__ __forceinline__ float gelu_erf(float v) {
     return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
 #else
     const float a = fminf(fabsf(v), kGeluClamp);
-    const float e = ex2_approx((a * kNegHalfLog2e) * a);
-    float p = kGeluNegR[0];
+    float p = kGeluL[0];
 #pragma unroll
-    for (int k = 1; k < kGeluTerms; ++k) p = fmaf(p, a, kGeluNegR[k]);
-    return fmaf(a * e, p, fmaxf(v, 0.0f));
+    for (int k = 1; k < kGeluTerms; ++k) p = fmaf(p, a, kGeluL[k]);
+    return fmaf(-a, ex2_approx(p), fmaxf(v, 0.0f));
 #endif
 }
 
@@ -79,12 +58,11 @@ __device__ __forceinline__ float2 gelu_erf2(float2 v) {
     return make_float2(gelu_erf(v.x), gelu_erf(v.y));
 #else
     const float2 a = make_float2(fminf(fabsf(v.x), kGeluClamp), fminf(fabsf(v.y), kGeluClamp));
-    const float2 s = __fmul2_rn(__fmul2_rn(a, make_float2(kNegHalfLog2e, kNegHalfLog2e)), a);
-    const float2 e = make_float2(ex2_approx(s.x), ex2_approx(s.y));
-    float2 p = make_float2(kGeluNegR[0], kGeluNegR[0]);
+    float2 p = make_float2(kGeluL[0], kGeluL[0]);
 #pragma unroll
-    for (int k = 1; k < kGeluTerms; ++k) p = __ffma2_rn(p, a, make_float2(kGeluNegR[k], kGeluNegR[k]));
-    return __ffma2_rn(__fmul2_rn(a, e), p, make_float2(fmaxf(v.x, 0.0f), fmaxf(v.y, 0.0f)));
+    for (int k = 1; k < kGeluTerms; ++k) p = __ffma2_rn(p, a, make_float2(kGeluL[k], kGeluL[k]));
+    const float2 e = make_float2(ex2_approx(p.x), ex2_approx(p.y));
+    return __ffma2_rn(make_float2(-a.x, -a.y), e, make_float2(fmaxf(v.x, 0.0f), fmaxf(v.y, 0.0f)));
 #endif
 }
 

@@ -69,6 +69,34 @@ def test_gemm(M, N, K, epi, act):
         assert rel(out32, base.double() + scale.double() * ref) < 1e-4
 
 
+def test_gelu_epilogue_accuracy():
+    """The erf-GELU of the GEMM epilogue on exact accumulators: A holds 65536 f16 values v in
+    [-8, 8] in its first column and every row of B selects that column, so the accumulator is v
+    exactly; the f32 output must be GELU(v) within 3.5e-7 (the bound of the evaluation) for
+    every v, and the f16 output within one f16 spacing of it."""
+    dev = "cuda:0"
+    vals = torch.linspace(-8, 8, 65536, dtype=torch.float64).half()
+    M, N, K = vals.numel(), 8, 16
+    A = torch.zeros(M, K, dtype=torch.float16, device=dev)
+    A[:, 0] = vals.to(dev)
+    B = torch.zeros(N, K, dtype=torch.float16, device=dev)
+    B[:, 0] = 1.0
+    bias = torch.zeros(N, device=dev)
+    ref = F.gelu(vals.double(), approximate="none")
+    out32 = torch.zeros(M, N, device=dev)
+    assert _lib().rfdetr_b200_op_gemm(_p(A), K, _p(B), K, M, N, K, 1, 1, _p(bias), None, None, None, 0.0, None, 0,
+                                      _p(out32), N, None, N, _stream()) == 0
+    out16 = torch.zeros(M, N, dtype=torch.float16, device=dev)
+    assert _lib().rfdetr_b200_op_gemm(_p(A), K, _p(B), K, M, N, K, 0, 1, _p(bias), None, None, None, 0.0, None, 0,
+                                      None, N, _p(out16), N, _stream()) == 0
+    torch.cuda.synchronize()
+    err32 = (out32.double().cpu() - ref[:, None]).abs().max().item()
+    assert err32 < 3.5e-7, err32
+    spacing = torch.from_numpy(np.spacing(np.abs(ref.half().numpy())).astype(np.float64))
+    err16 = (out16.double().cpu() - ref[:, None]).abs() / spacing[:, None]
+    assert err16.max().item() <= 1.0
+
+
 def _gemm_case(M, N, K, epi, act):
     """One rfdetr_b200_op_gemm call on seeded data against float64 torch."""
     torch.manual_seed(M * 7 + N + K)
