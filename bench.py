@@ -91,6 +91,13 @@ def headline_config(args, world):
             "image": S, "parallelism": f"dp{world} (independent replicas)", "l2": L2_NOTE}
 
 
+def smi_device(local):
+    """nvidia-smi's name for this rank's GPU: its entry of CUDA_VISIBLE_DEVICES (an index or a UUID,
+    both accepted by `nvidia-smi -i`) when that is set, else the local rank."""
+    vis = [x.strip() for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip()]
+    return vis[local] if local < len(vis) else str(local)
+
+
 class Clocks:
     """nvidia-smi sampling around the timed region.  The sampler is started
     before the warm-up and waited for (bounded) until its first sample, so a
@@ -461,7 +468,7 @@ def main():
     torch.cuda.synchronize()
 
     # ---- device-resident throughput --------------------------------------
-    ms_max, clk = leg.device(args.steps, warm, flush, pg, clocks=Clocks(local))
+    ms_max, clk = leg.device(args.steps, warm, flush, pg, clocks=Clocks(smi_device(local)))
     value = total * args.steps / (ms_max / 1000.0)
     launches = eng.kernels_per_forward() * args.steps
 

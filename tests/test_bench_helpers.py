@@ -75,3 +75,14 @@ def test_roofline_traffic_from_the_committed_profile():
     t = bench.traffic_from_profiles()
     assert t["bytes_per_launch"] == t["dram_read_bytes"] + t["dram_write_bytes"]
     assert 0 < t["bytes_per_launch"] <= t["algorithmic_bytes"]
+
+
+def test_clock_sampler_names_the_visible_gpu(monkeypatch):
+    import bench
+
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "3,5")
+    assert bench.smi_device(1) == "5"
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "GPU-aaaa, GPU-bbbb")
+    assert bench.smi_device(0) == "GPU-aaaa"
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
+    assert bench.smi_device(2) == "2"
