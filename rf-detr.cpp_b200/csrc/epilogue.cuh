@@ -126,6 +126,12 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int lane, int j) {
     return base + lane * 128 + ((j ^ (lane & 7)) << 4);
 }
 
+// The same for a 32-row x 64-byte box (64-byte swizzle: address bits 4-5 XOR bits 7-8): row
+// `lane` starts at byte lane * 64 and its 16-byte chunk j lands at chunk (j ^ ((lane >> 1) & 3)).
+__device__ __forceinline__ uint32_t swz64(uint32_t base, int lane, int j) {
+    return base + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);

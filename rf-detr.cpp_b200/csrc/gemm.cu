@@ -43,8 +43,14 @@ struct Cfg {
     static constexpr int B_ROWS = CTA2 ? BN / 2 : BN;
     static constexpr int NEPI = 8;  // epilogue warps: two per TMEM lane quadrant
     static constexpr int THREADS = 64 + 32 * NEPI;
+    // f16 outputs of the one-SM 192-wide tile stage through 32-row x 64-byte boxes (32 columns)
+    // instead of 128-byte ones: the 16 KB this frees holds a fifth operand stage, and the K = 384
+    // linears with this tile (the attention's qkv) are bound by the k-blocks in flight
+    static constexpr bool SMALL_BOX = EPI == EPI_F16 && BN == 192 && !CTA2;
+    static constexpr int BOX_BYTES = SMALL_BOX ? 2048 : 4096;  // per epilogue warp
     static constexpr int STAGES =
-        CTA2 ? (BN > 256 ? 4 : (BN >= 192 ? 6 : 8)) : (BN > 256 ? 3 : (BN >= 192 ? 4 : (BN == 128 ? 6 : 8)));
+        CTA2 ? (BN > 256 ? 4 : (BN >= 192 ? 6 : 8))
+             : (BN > 256 ? 3 : (SMALL_BOX ? 5 : (BN >= 192 ? 4 : (BN == 128 ? 6 : 8))));
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -54,7 +60,7 @@ struct Cfg {
     static constexpr int NSPLIT = BN > 256 ? 2 : 1;
     static constexpr int SLAB = BN / NSPLIT;
     static constexpr int HSLAB = B_ROWS / NSPLIT;
-    static constexpr int OUT_STAGE = NEPI * 4096;  // per epilogue warp: one 32-row x 128-byte box
+    static constexpr int OUT_STAGE = NEPI * BOX_BYTES;  // per epilogue warp: one 32-row box
     static constexpr int RED_BYTES = EPI == EPI_LN ? 1024 : 0;  // LN: per-row partial sums of 2 warps
     static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*align*/ + 256 /*barriers*/ + RED_BYTES;
     static_assert(SMEM <= 232448, "shared memory budget");
@@ -235,12 +241,12 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
         const int quad = warp & 3;         // TMEM lanes [32*quad, 32*quad + 32)
         const int half = e >> 2;           // which half of the tile's columns
         const int row_in_tile = quad * 32 + lane;
-        // staging: [quad][half] boxes of 4 KB; the LN path uses both halves of its quad
-        uint8_t* wptr = out_stage + quad * 8192 + half * 4096;
+        // staging: [quad][half] boxes of BOX_BYTES; the LN path uses both halves of its quad
+        uint8_t* wptr = out_stage + (quad * 2 + half) * C::BOX_BYTES;
         const uint32_t wbuf = smem_u32(wptr);
         constexpr bool kSplit = (EPI == EPI_LN) || (BN >= 128);
-        // first half: whole chunks (64 columns for f16 outputs, 32 for the f32 and patch paths)
-        constexpr int kChunk = EPI == EPI_F16 ? 64 : 32;
+        // first half: whole chunks (64 columns for f16 outputs with 128-byte boxes, else 32)
+        constexpr int kChunk = (EPI == EPI_F16 && !C::SMALL_BOX) ? 64 : 32;
         constexpr int kHalf0 = ((BN / 2 + kChunk - 1) / kChunk) * kChunk;
         const bool active = kSplit || half == 0;
         const int col_begin = kSplit ? half * kHalf0 : 0;
@@ -437,7 +443,35 @@ k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensor
                     }
                 }
             } else if (EPI != EPI_PATCH && p.tma_out) {
-                if constexpr (EPI == EPI_F16) {
+                if constexpr (EPI == EPI_F16 && C::SMALL_BOX) {
+                    // 32-column chunks: one 64-byte f16 box row per thread
+                    for (int c0 = col_begin; c0 < col_end; c0 += 32) {
+                        tmem_ld32(tbase + c0, raw);
+                        const int n0 = nt * BN + c0;
+                        float bj[32];
+                        load_cols<8>(bj, p.bias, n0, p.N, p.bias && n0 + 32 <= p.N && aligned16(p.bias + n0), 0.f);
+                        tmem_wait_ld();
+                        uint32_t h[16];
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const float2 w = act2<ACT>(__fadd2_rn(
+                                make_float2(__uint_as_float(raw[2 * q]), __uint_as_float(raw[2 * q + 1])),
+                                make_float2(bj[2 * q], bj[2 * q + 1])));
+                            h[q] = pack_half2(w.x, w.y);
+                        }
+                        if (lane == 0) bulk_wait_read<0>();
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            st_shared_v4(swz64(wbuf, lane, j), h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                        fence_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            if (n0 < p.N) tma_store_3d(&tmO16, wptr, n0, m0w, b);
+                            bulk_commit();
+                        }
+                    }
+                } else if constexpr (EPI == EPI_F16) {
                     // 64-column chunks: one 128-byte f16 box row per thread
                     for (int c0 = col_begin; c0 < col_end; c0 += 64) {
                         uint32_t raw2[32];
@@ -673,20 +707,21 @@ bool make_map(CUtensorMap* map, const void* base, int cols, long long rows, int 
     return r == CUDA_SUCCESS;
 }
 
-// 3-D output map (cols, rows, batch) with a 128-byte swizzled box of 32 rows.
+// 3-D output map (cols, rows, batch) with a swizzled box of 32 rows of `row_bytes` (128 or 64) bytes.
 bool make_out_map(CUtensorMap* map, const void* base, bool f16, int cols, int rows, int batches, int ld,
-                  long long batch_stride) {
+                  long long batch_stride, int row_bytes = 128) {
     const int esz = f16 ? 2 : 4;
     if (!base || ((uintptr_t)base & 15) || ((size_t)ld * esz) % 16) return false;
     if (batches > 1 && ((size_t)batch_stride * esz) % 16) return false;
     cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batches};
     cuuint64_t strides[2] = {(cuuint64_t)ld * esz,
                              (cuuint64_t)(batches > 1 ? batch_stride : (long long)ld * rows) * esz};
-    cuuint32_t box[3] = {(cuuint32_t)(128 / esz), 32, 1};
+    cuuint32_t box[3] = {(cuuint32_t)(row_bytes / esz), 32, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     return g_encode(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_NONE,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -739,7 +774,8 @@ cudaError_t launch(const GemmArgs& a_in, cudaStream_t st) {
     std::memset(&to16, 0, sizeof(to16));
     std::memset(&to32, 0, sizeof(to32));
     bool tma = EPI != EPI_PATCH && !CONV;  // CONV tiles hold fewer than 128 valid rows: direct stores
-    if (tma && a.out16) tma = make_out_map(&to16, a.out16, true, a.N, a.M, a.batches, a.ld16, a.out_batch_stride);
+    if (tma && a.out16)
+        tma = make_out_map(&to16, a.out16, true, a.N, a.M, a.batches, a.ld16, a.out_batch_stride, C::BOX_BYTES / 32);
     if (tma && a.out32) tma = make_out_map(&to32, a.out32, false, a.N, a.M, a.batches, a.ld32, a.out_batch_stride);
     a.tma_out = tma ? 1 : 0;
     a.patch_vec = (EPI == EPI_PATCH && a.N % 4 == 0 && a.ld32 % 4 == 0 && !((uintptr_t)a.out32 & 15) &&
