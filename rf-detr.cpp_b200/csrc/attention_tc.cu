@@ -594,6 +594,239 @@ k_attn_tc_items(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
 }
 
+// 128-key blocks for long sequences (the global blocks): S = Q K^T of a block is M=128 x N=128,
+// and P goes back into TMEM as packed f16 (tcgen05.st), from where the P V product reads it as its
+// A operand.  The per-block hand-off (S ready, S read, P ready, P V done) is paid once per 128 keys
+// instead of once per 64, and without a P tile in shared memory a CTA holds Q (16 KB) and two-slot
+// K and V rings of 128-key tiles (64 KB), so two CTAs still fit per SM.
+//   TMEM (256 columns): S [0,128) f32, O [128,192) f32, P [192,256) f16 pairs.
+//   K and V slots have their own barriers: K_j's slot is released when S_j is computed, V_j's
+//   when P_j V_j is, so the next K tiles load while the softmax of the current block runs.
+//   The final O / l staging box of each lane quadrant is its quarter of Q's tile (free once the
+//   last S product has completed).
+constexpr int AK2 = 128;                  // keys per block
+constexpr int KV2_BYTES = AK2 * HD * 2;   // 16 KB
+constexpr int NS2 = 2;                    // ring slots
+constexpr int SMEM2_TILES = Q_BYTES + 2 * NS2 * KV2_BYTES;
+constexpr int SMEM2 = SMEM2_TILES + 1024 + 256;
+constexpr int TMEM2_COLS = 256;
+
+__global__ void __launch_bounds__(192, 2)
+k_attn_tc128(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, int L, float sl2,
+             int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + Q_BYTES;              // NS2 slots
+    uint8_t* sV = sK + NS2 * KV2_BYTES;      // NS2 slots
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM2_TILES);
+    uint64_t* q_full = bars + 0;
+    uint64_t* k_full = bars + 1;               // [NS2]
+    uint64_t* k_empty = k_full + NS2;          // [NS2]
+    uint64_t* v_full = k_empty + NS2;          // [NS2]
+    uint64_t* v_empty = v_full + NS2;          // [NS2]
+    uint64_t* s_full = v_empty + NS2;
+    uint64_t* s_free = s_full + 1;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* pv_done = s_full + 3;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_full + 4);
+    volatile int* cta_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * AQ;
+    const int head = blockIdx.y;
+    const int g = blockIdx.z;
+    const int nb = (L + AK2 - 1) / AK2;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < NS2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 128);
+        mbar_init(p_full, 128);
+        mbar_init(pv_done, 1);
+        *cta_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_holder, TMEM2_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    const uint32_t tS = tmem, tO = tmem + AK2, tP = tmem + AK2 + HD;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            mbar_arrive_expect_tx(q_full, Q_BYTES);
+            tma_load_3d(&tmQ, q_full, sQ, head * HD, q0, g);
+            for (int j = 0; j < nb; ++j) {
+                const int slot = j % NS2;
+                const uint32_t ph = ((j / NS2) & 1) ^ 1;
+                if (!mbar_wait(&k_empty[slot], ph, cta_abort, err)) break;
+                mbar_arrive_expect_tx(&k_full[slot], KV2_BYTES);
+                tma_load_3d(&tmK, &k_full[slot], sK + slot * KV2_BYTES, head * HD, j * AK2, g);
+                if (!mbar_wait(&v_empty[slot], ph, cta_abort, err)) break;
+                mbar_arrive_expect_tx(&v_full[slot], KV2_BYTES);
+                tma_load_3d(&tmV, &v_full[slot], sV + slot * KV2_BYTES, head * HD, j * AK2, g);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t IDESC_S = idesc_f16_f32(AQ, AK2);
+            constexpr uint32_t IDESC_PV = idesc_f16_f32(AQ, HD) | (1u << 16);  // B (V) MN-major
+            const uint32_t q_s = smem_u32(sQ);
+            auto issue_s = [&](int j) -> bool {
+                const int slot = j % NS2;
+                if (!mbar_wait(&k_full[slot], (j / NS2) & 1, cta_abort, err)) return false;
+                tc_fence_after();
+                const uint32_t k_s = smem_u32(sK + slot * KV2_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    umma_f16(tS, sw128_kmajor_desc(q_s + kk * 32), sw128_kmajor_desc(k_s + kk * 32), IDESC_S, kk > 0);
+                umma_commit(s_full);
+                umma_commit(&k_empty[slot]);
+                return true;
+            };
+            bool ok = mbar_wait(q_full, 0, cta_abort, err) && issue_s(0);
+            for (int j = 0; ok && j < nb; ++j) {
+                const int slot = j % NS2;
+                if (j + 1 < nb) {
+                    if (!mbar_wait(s_free, j & 1, cta_abort, err) || !issue_s(j + 1)) break;
+                }
+                if (!mbar_wait(p_full, j & 1, cta_abort, err)) break;
+                if (!mbar_wait(&v_full[slot], (j / NS2) & 1, cta_abort, err)) break;
+                tc_fence_after();
+                const uint32_t v_s = smem_u32(sV + slot * KV2_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < AK2 / 16; ++kk)
+                    umma_f16_ts(tO, tP + kk * 8, sw128_kmajor_desc(v_s + kk * 2048), IDESC_PV,
+                                (j > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(pv_done);
+                umma_commit(&v_empty[slot]);
+            }
+        }
+    } else {
+        // ---- softmax warps: thread = query row (q0 + quad*32 + lane)
+        const int quad = warp & 3;
+        const uint32_t lanebase = (uint32_t)(quad * 32) << 16;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nb; ++j) {
+            if (!mbar_wait(s_full, j & 1, cta_abort, err)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t r[4][32];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) tmem_ld32(tS + lanebase + 32 * h, r[h]);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(s_free);
+            const int kbase = j * AK2;
+            if (kbase + AK2 > L) {
+#pragma unroll
+                for (int h = 0; h < 4; ++h)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (kbase + 32 * h + e >= L) r[h][e] = __float_as_uint(-INFINITY);
+            }
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // row max of raw scores
+#pragma unroll
+            for (int h = 0; h < 4; h += 2)
+#pragma unroll
+                for (int e = 0; e < 32; ++e)
+                    mx4[e & 3] = fmax3(mx4[e & 3], __uint_as_float(r[h][e]), __uint_as_float(r[h + 1][e]));
+            // scale > 0 commutes with max; running max in log2 units
+            const float m_cand = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2);
+            const float m_new = m_cand > m + kRescaleLog2 ? m_cand : m;  // always taken on the first block
+            const float alpha = ex2(m - m_new);  // 1 while the reference holds; 0 on the first block
+            float2 rs2 = make_float2(0.f, 0.f);
+            const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_new, -m_new);
+            uint32_t p[2][32];  // P row as f16 pairs: column c holds keys 2c, 2c + 1
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[h][e]), __uint_as_float(r[h][e + 1])),
+                                                sl2v, negm);
+                    // RFB_ATTN_FMA_EXP of every 8 key pairs take their exponentials on the FMA pipe
+                    const bool on_fma = ((e >> 1) & 7) >= 8 - RFB_ATTN_FMA_EXP;
+                    const float2 pa = on_fma ? exp2_fma2(a) : make_float2(ex2(a.x), ex2(a.y));
+                    rs2 = __fadd2_rn(rs2, pa);
+                    p[h >> 1][(h & 1) * 16 + (e >> 1)] = pack_half2(pa.x, pa.y);
+                }
+            }
+            l = l * alpha + (rs2.x + rs2.y);
+            m = m_new;
+            if (j > 0) {
+                // previous P V done: P columns reusable, O stable for the rescale
+                if (!mbar_wait(pv_done, (j - 1) & 1, cta_abort, err)) { ok = false; break; }
+                tc_fence_after();
+            }
+            tmem_st32(tP + lanebase, p[0]);
+            tmem_st32(tP + lanebase + 32, p[1]);
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+                uint32_t o[32];
+#pragma unroll
+                for (int c = 0; c < HD; c += 32) {
+                    tmem_ld32(tO + lanebase + c, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float2 y = __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])),
+                                                    make_float2(alpha, alpha));
+                        o[e] = __float_as_uint(y.x);
+                        o[e + 1] = __float_as_uint(y.y);
+                    }
+                    tmem_st32(tO + lanebase + c, o);
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && mbar_wait(pv_done, (nb - 1) & 1, cta_abort, err)) {
+            tc_fence_after();
+            const float inv = 1.0f / l;
+            // stage O / l as f16 in this warp's quarter of Q's tile (every S product has completed)
+            uint8_t* stage = sQ + quad * 4096;
+            const uint32_t st_s = smem_u32(stage);
+            uint32_t o[32];
+#pragma unroll
+            for (int c = 0; c < HD; c += 32) {
+                tmem_ld32(tO + lanebase + c, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    st_shared_v4(swz(st_s, lane, (c >> 3) + q),
+                                 pack_half2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                 pack_half2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                 pack_half2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                 pack_half2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_3d(&tmO, stage, head * HD, q0 + quad * 32, g);
+                bulk_commit();
+                bulk_wait<0>();
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM2_COLS);
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
 std::once_flag g_enc_once;
 
@@ -639,11 +872,26 @@ cudaError_t attention_tc(const __half* q, const __half* k, const __half* v, int 
             e = cudaFuncSetAttribute(k_attn_tc_items<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<2>::SMEM);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_attn_tc_items<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<4>::SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_attn_tc128, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
     const int cols = heads * HD;
     CUtensorMap mq, mk, mv, mo;
+    // long sequences: 128-key blocks with P in TMEM (RFDETR_ATTN_KB=64 keeps the 64-key kernels)
+    const char* kbenv = std::getenv("RFDETR_ATTN_KB");
+    const bool wide_keys = seq_len > RFB_ATTN_SHORT_KEYS && !(kbenv && std::atoi(kbenv) == 64);
+    if (wide_keys) {
+        if (!make_seq_map(&mq, q, cols, seq_len, groups, ldq, AQ) ||
+            !make_seq_map(&mk, k, cols, seq_len, groups, ldk, AK2) ||
+            !make_seq_map(&mv, v, cols, seq_len, groups, ldv, AK2) ||
+            !make_seq_map(&mo, o, cols, seq_len, groups, ldo, 32))
+            return cudaErrorInvalidValue;
+        const dim3 grid2((seq_len + AQ - 1) / AQ, heads, groups);
+        k_attn_tc128<<<grid2, 192, SMEM2, st>>>(mq, mk, mv, mo, seq_len, scale * 1.4426950408889634f, err);
+        return cudaGetLastError();
+    }
     if (!make_seq_map(&mq, q, cols, seq_len, groups, ldq, AQ) || !make_seq_map(&mk, k, cols, seq_len, groups, ldk, AK) ||
         !make_seq_map(&mv, v, cols, seq_len, groups, ldv, AK) || !make_seq_map(&mo, o, cols, seq_len, groups, ldo, 32))
         return cudaErrorInvalidValue;

@@ -206,6 +206,19 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, issued by one thread.  A (M = 128) has its row i
+// in TMEM lane i and two f16 elements of K per 32-bit column (element 2c in the low half of column
+// c), so one K = 16 step reads 8 columns.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Two warps (64 threads, e.g. the two that share a TMEM lane quadrant) meet
 // at the mbarrier `bar` (initialised with count 64); bounded like every other
 // wait.  Returns false (warp-uniformly) when the CTA is unwinding.

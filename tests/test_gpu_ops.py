@@ -187,6 +187,15 @@ def test_attention(L, groups, heads, hd):
     assert rel(o, ref) < 4e-3
 
 
+@pytest.mark.parametrize("L", [1616, 150, 129])
+def test_attention_64_key_blocks(L, monkeypatch):
+    """Sequences longer than 128 keys run in 128-key blocks with P in TMEM by default; the 64-key
+    kernel (P in shared memory) stays selectable with RFDETR_ATTN_KB=64 and gives the same softmax."""
+    monkeypatch.setenv("RFDETR_ATTN_KB", "64")
+    test_attention(L, 2, 6, 64)
+    test_attention_growing_max(L)
+
+
 @pytest.mark.parametrize("L", [1616, 150, 700])
 def test_attention_growing_max(L):
     """Scores whose row maximum keeps growing along the keys, so the lazily
