@@ -879,9 +879,11 @@ cudaError_t attention_tc(const __half* q, const __half* k, const __half* v, int 
     }
     const int cols = heads * HD;
     CUtensorMap mq, mk, mv, mo;
-    // long sequences: 128-key blocks with P in TMEM (RFDETR_ATTN_KB=64 keeps the 64-key kernels)
+    // long sequences: 128-key blocks with P in TMEM (RFDETR_ATTN_KB=64 keeps the 64-key kernels,
+    // =128 takes the 128-key kernel for short sequences too)
     const char* kbenv = std::getenv("RFDETR_ATTN_KB");
-    const bool wide_keys = seq_len > RFB_ATTN_SHORT_KEYS && !(kbenv && std::atoi(kbenv) == 64);
+    const int kb = kbenv ? std::atoi(kbenv) : 0;
+    const bool wide_keys = kb == 128 || (seq_len > RFB_ATTN_SHORT_KEYS && kb != 64);
     if (wide_keys) {
         if (!make_seq_map(&mq, q, cols, seq_len, groups, ldq, AQ) ||
             !make_seq_map(&mk, k, cols, seq_len, groups, ldk, AK2) ||
