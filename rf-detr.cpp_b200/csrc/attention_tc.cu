@@ -1,5 +1,7 @@
 // Fused multi-head attention on the 5th-generation tensor cores (head_dim 64):
-// the windowed and global blocks of the DINOv2 backbone.
+// the windowed and global blocks of the DINOv2 backbone.  Sequences longer than
+// 128 tokens (the global blocks) run k_attn_tc128 (128-key blocks, P kept in
+// TMEM; described above that kernel); the windows run the 64-key kernels below.
 //
 // One CTA = 128 query rows of one (group, head); keys in blocks of 64.
 //   warp 0      TMA: Q once, then K/V blocks into a 4-slot ring (3-D tensor
